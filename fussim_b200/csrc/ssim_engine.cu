@@ -1,0 +1,449 @@
+// C ABI of the B200 SSIM engine: argument checks, launch configuration, dispatch over
+// window size / element types, and the extern "C" entry points declared in
+// include/fussim_b200.h. No torch, no Python: any host language can bind this library.
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "fussim_b200.h"
+#include "ssim_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+std::string window_message(int ws) {
+  // Same text as the reference's dispatch (csrc/ssim.cu:617).
+  return "window_size must be 7, 9, or 11, got " + std::to_string(ws);
+}
+
+int check_window(int ws) {
+  if (ws == 7 || ws == 9 || ws == 11) return FSSIM_OK;
+  return fail(FSSIM_ERR_WINDOW, window_message(ws));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Shape checks shared by every entry point. Rows and columns are 32-bit inside the kernels.
+int check_shape(int64_t B, int64_t C, int64_t H, int64_t W) {
+  if (B < 0 || C < 0 || H < 0 || W < 0) return fail(FSSIM_ERR_SHAPE, "negative dimension");
+  if (H > (INT_MAX / 2) || W > (INT_MAX / 2) || C > INT_MAX || B > INT_MAX)
+    return fail(FSSIM_ERR_SHAPE, "dimension too large (H, W must be < 2^30)");
+  const double n = static_cast<double>(B) * C * H * W;
+  if (n > 4.0e18) return fail(FSSIM_ERR_SHAPE, "B*C*H*W overflows int64");
+  return FSSIM_OK;
+}
+
+fssim::Geometry make_geometry(int64_t B, int64_t C, int64_t H, int64_t W) {
+  fssim::Geometry g;
+  g.H = H;
+  g.W = W;
+  g.HW = H * W;
+  g.S = static_cast<int>((W + fssim::kStrip - 1) / fssim::kStrip);
+  g.C = static_cast<int>(C);
+  g.B = static_cast<int>(B);
+  g.LT = B * C * static_cast<int64_t>(g.S) * H;
+  return g;
+}
+
+int device_sms(int* sms) {
+  static std::mutex mu;
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(FSSIM_ERR_CUDA, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == 0) {
+    int v = 0;
+    e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess)
+      return fail(FSSIM_ERR_CUDA, std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e));
+    cached[dev] = v;
+  }
+  *sms = cached[dev];
+  return FSSIM_OK;
+}
+
+// Opt a kernel in to its dynamic shared memory size on the current device and return the
+// number of resident CTAs per SM. `cache` is owned by one kernel instantiation (it lives in
+// the launch_* template below), so every instantiation gets its own per-device entry.
+template <typename Kernel>
+int kernel_occupancy(Kernel k, size_t smem, int (&cache)[64], std::mutex& mu, int* occ) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(FSSIM_ERR_CUDA, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) {
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess)
+      return fail(FSSIM_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    int v = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k, fssim::kThreads, smem);
+    if (e != cudaSuccess || v <= 0)
+      return fail(FSSIM_ERR_CUDA, std::string("occupancy query failed: ") + cudaGetErrorString(e));
+    cache[dev] = v;
+  }
+  *occ = cache[dev];
+  return FSSIM_OK;
+}
+
+// Persistent grid: one CTA per resident slot, but no CTA with fewer than ~2 steps of rows.
+int grid_size(const fssim::Geometry& g, int occ, int sms) {
+  const int64_t slots = static_cast<int64_t>(occ) * sms;
+  const int64_t by_work = (g.LT + 2 * fssim::kRows - 1) / (2 * fssim::kRows);
+  int64_t grid = slots < by_work ? slots : by_work;
+  if (grid < 1) grid = 1;
+  return static_cast<int>(grid);
+}
+
+int launch_error(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return FSSIM_OK;
+}
+
+template <int HALO, typename TIn, typename TP, bool TRAIN>
+int launch_fwd(const fssim::FwdParams& p, cudaStream_t stream) {
+  using Cfg = fssim::FwdConfig<HALO, TIn, TP, TRAIN>;
+  auto k = fssim::ssim_fwd_kernel<HALO, TIn, TP, TRAIN>;
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int occ = 0, sms = 0;
+  int st = kernel_occupancy(k, Cfg::kSmem, cache, mu, &occ);
+  if (st) return st;
+  st = device_sms(&sms);
+  if (st) return st;
+  const int grid = grid_size(p.g, occ, sms);
+  k<<<grid, fssim::kThreads, Cfg::kSmem, stream>>>(p);
+  return launch_error("ssim forward launch");
+}
+
+template <int HALO, typename TIn, typename TP, bool DLMAP>
+int launch_bwd(const fssim::BwdParams& p, cudaStream_t stream) {
+  using Cfg = fssim::BwdConfig<HALO, TIn, TP, DLMAP>;
+  auto k = fssim::ssim_bwd_kernel<HALO, TIn, TP, DLMAP>;
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int occ = 0, sms = 0;
+  int st = kernel_occupancy(k, Cfg::kSmem, cache, mu, &occ);
+  if (st) return st;
+  st = device_sms(&sms);
+  if (st) return st;
+  const int grid = grid_size(p.g, occ, sms);
+  k<<<grid, fssim::kThreads, Cfg::kSmem, stream>>>(p);
+  return launch_error("ssim backward launch");
+}
+
+template <typename TIn, typename TP, bool TRAIN>
+int dispatch_fwd(int ws, const fssim::FwdParams& p, cudaStream_t s) {
+  switch (ws) {
+    case 7: return launch_fwd<3, TIn, TP, TRAIN>(p, s);
+    case 9: return launch_fwd<4, TIn, TP, TRAIN>(p, s);
+    case 11: return launch_fwd<5, TIn, TP, TRAIN>(p, s);
+    default: return fail(FSSIM_ERR_WINDOW, window_message(ws));
+  }
+}
+
+template <typename TIn, typename TP, bool DLMAP>
+int dispatch_bwd(int ws, const fssim::BwdParams& p, cudaStream_t s) {
+  switch (ws) {
+    case 7: return launch_bwd<3, TIn, TP, DLMAP>(p, s);
+    case 9: return launch_bwd<4, TIn, TP, DLMAP>(p, s);
+    case 11: return launch_bwd<5, TIn, TP, DLMAP>(p, s);
+    default: return fail(FSSIM_ERR_WINDOW, window_message(ws));
+  }
+}
+
+size_t elem_size(int dt) { return dt == FSSIM_F32 ? 4 : 2; }
+
+__global__ void fill_kernel(float* out, int64_t n, float v) {
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) out[i] = v;
+}
+
+// Map-producing forward shared by the FP32 and FP16 reference entry points.
+template <typename TIn>
+int compat_forward(int ws, float C1, float C2, const TIn* img1, const TIn* img2, int64_t B,
+                   int64_t C, int64_t H, int64_t W, bool train, float* map, float* p0, float* p1,
+                   float* p2, cudaStream_t stream) {
+  g_last_error.clear();
+  int st = check_window(ws);
+  if (st) return st;
+  st = check_shape(B, C, H, W);
+  if (st) return st;
+  if (B * C * H * W == 0) return FSSIM_OK;
+  if (!img1 || !img2 || !map) return fail(FSSIM_ERR_NULLPTR, "img1, img2 and ssim_map are required");
+  if (train && (!p0 || !p1 || !p2))
+    return fail(FSSIM_ERR_NULLPTR, "train requires dm_dmu1, dm_dsigma1_sq and dm_dsigma12");
+  constexpr int64_t E = 16 / sizeof(TIn);
+  fssim::FwdParams p{};
+  p.img1 = img1;
+  p.img2 = img2;
+  p.map = map;
+  p.p0 = p0;
+  p.p1 = p1;
+  p.p2 = p2;
+  p.g = make_geometry(B, C, H, W);
+  p.C1 = C1;
+  p.C2 = C2;
+  p.out_scale = 1.f;
+  p.valid = 0;
+  p.clamp = 0;
+  p.reduce = FSSIM_REDUCE_NONE;
+  p.mask_partials = 0;
+  p.aligned16 = (W % E == 0) && aligned(img1, 16) && aligned(img2, 16);
+  p.pair_ok = (W % 2 == 0) && aligned(map, 8) &&
+              (!train || (aligned(p0, 8) && aligned(p1, 8) && aligned(p2, 8)));
+  if (train) return dispatch_fwd<TIn, float, true>(ws, p, stream);
+  return dispatch_fwd<TIn, float, false>(ws, p, stream);
+}
+
+template <typename TIn>
+int compat_backward(int ws, const TIn* img1, const TIn* img2, const float* dl, const float* p0,
+                    const float* p1, const float* p2, int64_t B, int64_t C, int64_t H, int64_t W,
+                    float* grad, cudaStream_t stream) {
+  g_last_error.clear();
+  int st = check_window(ws);
+  if (st) return st;
+  st = check_shape(B, C, H, W);
+  if (st) return st;
+  if (B * C * H * W == 0) return FSSIM_OK;
+  if (!img1 || !img2 || !dl || !p0 || !p1 || !p2 || !grad)
+    return fail(FSSIM_ERR_NULLPTR, "all tensors of fusedssim_backward are required");
+  fssim::BwdParams p{};
+  p.img1 = img1;
+  p.img2 = img2;
+  p.p0 = p0;
+  p.p1 = p1;
+  p.p2 = p2;
+  p.dl = dl;
+  p.grad_out = nullptr;
+  p.grad = grad;
+  p.g = make_geometry(B, C, H, W);
+  p.chain_scale = 1.f;
+  p.grad_per_image = 0;
+  p.grad_dtype = FSSIM_F32;
+  p.aligned16 = (W % 4 == 0) && aligned(dl, 16) && aligned(p0, 16) && aligned(p1, 16) &&
+                aligned(p2, 16);
+  p.pair_ok = (W % 2 == 0) && aligned(img1, 2 * sizeof(TIn)) && aligned(img2, 2 * sizeof(TIn)) &&
+              aligned(grad, 8);
+  return dispatch_bwd<TIn, float, true>(ws, p, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fssim_status_string(int status) {
+  switch (status) {
+    case FSSIM_OK: return "success";
+    case FSSIM_ERR_WINDOW: return "unsupported window size";
+    case FSSIM_ERR_SHAPE: return "invalid shape";
+    case FSSIM_ERR_DTYPE: return "unsupported element type";
+    case FSSIM_ERR_NULLPTR: return "required pointer is NULL";
+    case FSSIM_ERR_WORKSPACE: return "workspace missing or too small";
+    case FSSIM_ERR_CUDA: return "CUDA error";
+    case FSSIM_ERR_ARGUMENT: return "invalid argument";
+    default: return "unknown status";
+  }
+}
+
+const char* fssim_last_error(void) { return g_last_error.c_str(); }
+
+const char* fssim_version(void) { return "0.1.0"; }
+
+int fssim_fusedssim(int window_size, float C1, float C2, const float* img1, const float* img2,
+                    int64_t B, int64_t C, int64_t H, int64_t W, int train, float* ssim_map,
+                    float* dm_dmu1, float* dm_dsigma1_sq, float* dm_dsigma12,
+                    fssim_stream_t stream) {
+  return compat_forward<float>(window_size, C1, C2, img1, img2, B, C, H, W, train != 0, ssim_map,
+                               dm_dmu1, dm_dsigma1_sq, dm_dsigma12, stream);
+}
+
+int fssim_fusedssim_backward(int window_size, float C1, float C2, const float* img1,
+                             const float* img2, const float* dL_dmap, const float* dm_dmu1,
+                             const float* dm_dsigma1_sq, const float* dm_dsigma12, int64_t B,
+                             int64_t C, int64_t H, int64_t W, float* dL_dimg1,
+                             fssim_stream_t stream) {
+  (void)C1;
+  (void)C2;  // the backward needs only the partials, as in the reference
+  return compat_backward<float>(window_size, img1, img2, dL_dmap, dm_dmu1, dm_dsigma1_sq,
+                                dm_dsigma12, B, C, H, W, dL_dimg1, stream);
+}
+
+int fssim_fusedssim_fp16(int window_size, float C1, float C2, const uint16_t* img1,
+                         const uint16_t* img2, int64_t B, int64_t C, int64_t H, int64_t W,
+                         float* ssim_map, fssim_stream_t stream) {
+  return compat_forward<__half>(window_size, C1, C2, reinterpret_cast<const __half*>(img1),
+                                reinterpret_cast<const __half*>(img2), B, C, H, W, false,
+                                ssim_map, nullptr, nullptr, nullptr, stream);
+}
+
+int fssim_fusedssim_fp16_train(int window_size, float C1, float C2, const uint16_t* img1,
+                               const uint16_t* img2, int64_t B, int64_t C, int64_t H,
+                               int64_t W, float* ssim_map, float* dm_dmu1,
+                               float* dm_dsigma1_sq, float* dm_dsigma12,
+                               fssim_stream_t stream) {
+  return compat_forward<__half>(window_size, C1, C2, reinterpret_cast<const __half*>(img1),
+                                reinterpret_cast<const __half*>(img2), B, C, H, W, true,
+                                ssim_map, dm_dmu1, dm_dsigma1_sq, dm_dsigma12, stream);
+}
+
+int fssim_fusedssim_fp16_backward(int window_size, float C1, float C2, const uint16_t* img1,
+                                  const uint16_t* img2, const float* dL_dmap,
+                                  const float* dm_dmu1, const float* dm_dsigma1_sq,
+                                  const float* dm_dsigma12, int64_t B, int64_t C, int64_t H,
+                                  int64_t W, float* dL_dimg1, fssim_stream_t stream) {
+  (void)C1;
+  (void)C2;
+  return compat_backward<__half>(window_size, reinterpret_cast<const __half*>(img1),
+                                 reinterpret_cast<const __half*>(img2), dL_dmap, dm_dmu1,
+                                 dm_dsigma1_sq, dm_dsigma12, B, C, H, W, dL_dimg1, stream);
+}
+
+size_t fssim_forward_workspace_bytes(int64_t B) {
+  if (B <= 0) return 256;
+  return 256 + static_cast<size_t>(B) * sizeof(unsigned long long);
+}
+
+int fssim_forward(const fssim_forward_args* a, fssim_stream_t stream) {
+  g_last_error.clear();
+  if (!a) return fail(FSSIM_ERR_NULLPTR, "args is NULL");
+  int st = check_window(a->window_size);
+  if (st) return st;
+  st = check_shape(a->B, a->C, a->H, a->W);
+  if (st) return st;
+  if (a->dtype != FSSIM_F32 && a->dtype != FSSIM_F16)
+    return fail(FSSIM_ERR_DTYPE, "img dtype must be F32 or F16");
+  if (a->train && !(a->partial_dtype == FSSIM_F32 ||
+                    (a->partial_dtype == FSSIM_F16 && a->dtype == FSSIM_F16)))
+    return fail(FSSIM_ERR_DTYPE, "partials must be F32 (or F16 with F16 images)");
+  if (a->reduce < FSSIM_REDUCE_NONE || a->reduce > FSSIM_REDUCE_PER_IMAGE)
+    return fail(FSSIM_ERR_ARGUMENT, "reduce must be 0, 1 or 2");
+  const int64_t N = a->B * a->C * a->H * a->W;
+  if (a->reduce != FSSIM_REDUCE_NONE) {
+    if (!a->out) return fail(FSSIM_ERR_NULLPTR, "out is required when reducing");
+    if (!a->workspace || a->workspace_bytes < fssim_forward_workspace_bytes(a->B))
+      return fail(FSSIM_ERR_WORKSPACE, "workspace smaller than fssim_forward_workspace_bytes(B)");
+    if (!aligned(a->workspace, 16)) return fail(FSSIM_ERR_WORKSPACE, "workspace must be 16-byte aligned");
+  }
+  if (N == 0) {
+    // Nothing to reduce: sums are 0 and out = 0 * out_scale (NaN for a mean over no pixels,
+    // out_scale = 1/0), which is what torch's mean of an empty tensor gives.
+    if (a->reduce != FSSIM_REDUCE_NONE) {
+      const int64_t n_out = a->reduce == FSSIM_REDUCE_SCALAR ? 1 : a->B;
+      if (n_out > 0) {
+        fill_kernel<<<1, 128, 0, stream>>>(a->out, n_out, 0.f * a->out_scale);
+        const int e = launch_error("fill launch");
+        if (e) return e;
+      }
+      if (a->image_sums && a->B > 0) {
+        const cudaError_t e = cudaMemsetAsync(a->image_sums, 0, sizeof(double) * a->B, stream);
+        if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, cudaGetErrorString(e));
+      }
+    }
+    return FSSIM_OK;
+  }
+  if (!a->img1 || !a->img2) return fail(FSSIM_ERR_NULLPTR, "img1 and img2 are required");
+  if (a->train && !a->partials) return fail(FSSIM_ERR_NULLPTR, "train requires partials");
+
+  const size_t E = elem_size(a->dtype);
+  const size_t PE = elem_size(a->partial_dtype);
+  fssim::FwdParams p{};
+  p.img1 = a->img1;
+  p.img2 = a->img2;
+  p.map = a->ssim_map;
+  if (a->train) {
+    char* base = static_cast<char*>(a->partials);
+    p.p0 = base;
+    p.p1 = base + static_cast<size_t>(N) * PE;
+    p.p2 = base + 2 * static_cast<size_t>(N) * PE;
+  }
+  p.out = a->out;
+  p.image_sums = a->image_sums;
+  if (a->reduce != FSSIM_REDUCE_NONE) {
+    p.ticket = static_cast<unsigned*>(a->workspace);
+    p.acc = reinterpret_cast<unsigned long long*>(static_cast<char*>(a->workspace) + 256);
+  }
+  p.g = make_geometry(a->B, a->C, a->H, a->W);
+  p.C1 = a->C1;
+  p.C2 = a->C2;
+  p.out_scale = a->out_scale;
+  p.valid = a->valid ? 1 : 0;
+  p.clamp = a->clamp ? 1 : 0;
+  p.reduce = a->reduce;
+  p.mask_partials = 1;
+  p.aligned16 = (a->W % static_cast<int64_t>(16 / E) == 0) && aligned(a->img1, 16) &&
+                aligned(a->img2, 16);
+  bool pair = (a->W % 2 == 0) && (!a->ssim_map || aligned(a->ssim_map, 8));
+  if (a->train) pair = pair && aligned(p.p0, 2 * PE) && aligned(p.p1, 2 * PE) && aligned(p.p2, 2 * PE);
+  p.pair_ok = pair;
+
+  const int ws = a->window_size;
+  cudaStream_t s = stream;
+  if (a->dtype == FSSIM_F32) {
+    if (a->train) return dispatch_fwd<float, float, true>(ws, p, s);
+    return dispatch_fwd<float, float, false>(ws, p, s);
+  }
+  if (!a->train) return dispatch_fwd<__half, float, false>(ws, p, s);
+  if (a->partial_dtype == FSSIM_F16) return dispatch_fwd<__half, __half, true>(ws, p, s);
+  return dispatch_fwd<__half, float, true>(ws, p, s);
+}
+
+int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
+  g_last_error.clear();
+  if (!a) return fail(FSSIM_ERR_NULLPTR, "args is NULL");
+  int st = check_window(a->window_size);
+  if (st) return st;
+  st = check_shape(a->B, a->C, a->H, a->W);
+  if (st) return st;
+  if (a->dtype != FSSIM_F32 && a->dtype != FSSIM_F16)
+    return fail(FSSIM_ERR_DTYPE, "img dtype must be F32 or F16");
+  if (!(a->partial_dtype == FSSIM_F32 || (a->partial_dtype == FSSIM_F16 && a->dtype == FSSIM_F16)))
+    return fail(FSSIM_ERR_DTYPE, "partials must be F32 (or F16 with F16 images)");
+  if (a->grad_dtype < FSSIM_F32 || a->grad_dtype > FSSIM_BF16)
+    return fail(FSSIM_ERR_DTYPE, "grad dtype must be F32, F16 or BF16");
+  const int64_t N = a->B * a->C * a->H * a->W;
+  if (N == 0) return FSSIM_OK;
+  if (!a->img1 || !a->img2 || !a->partials || !a->grad)
+    return fail(FSSIM_ERR_NULLPTR, "img1, img2, partials and grad are required");
+  const size_t E = elem_size(a->dtype);
+  const size_t PE = elem_size(a->partial_dtype);
+  const size_t GE = elem_size(a->grad_dtype);
+  const char* base = static_cast<const char*>(a->partials);
+  fssim::BwdParams p{};
+  p.img1 = a->img1;
+  p.img2 = a->img2;
+  p.p0 = base;
+  p.p1 = base + static_cast<size_t>(N) * PE;
+  p.p2 = base + 2 * static_cast<size_t>(N) * PE;
+  p.dl = nullptr;
+  p.grad_out = a->grad_out;
+  p.grad = a->grad;
+  p.g = make_geometry(a->B, a->C, a->H, a->W);
+  p.chain_scale = a->chain_scale;
+  p.grad_per_image = a->grad_out_per_image ? 1 : 0;
+  p.grad_dtype = a->grad_dtype;
+  p.aligned16 = (a->W % static_cast<int64_t>(16 / PE) == 0) && aligned(p.p0, 16) &&
+                aligned(p.p1, 16) && aligned(p.p2, 16);
+  p.pair_ok = (a->W % 2 == 0) && aligned(a->img1, 2 * E) && aligned(a->img2, 2 * E) &&
+              aligned(a->grad, 2 * GE);
+  const int ws = a->window_size;
+  cudaStream_t s = stream;
+  if (a->dtype == FSSIM_F32) return dispatch_bwd<float, float, false>(ws, p, s);
+  if (a->partial_dtype == FSSIM_F16) return dispatch_bwd<__half, __half, false>(ws, p, s);
+  return dispatch_bwd<__half, float, false>(ws, p, s);
+}
+
+}  // extern "C"

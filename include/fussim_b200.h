@@ -1,0 +1,177 @@
+/*
+ * fussim_b200 — C ABI of the B200 SSIM loss engine.
+ *
+ * Plain pointers and sizes only; no C++ or torch types cross this boundary. Every
+ * entry point is asynchronous on the given stream, never throws, and returns a
+ * fssim_status (0 = success). Tensors are dense NCHW (B, C, H, W) in device memory,
+ * element offsets computed in 64-bit.
+ *
+ * Two families of entry points:
+ *
+ *  1. The five reference extension functions of OpsiClear/fussim, one C function each,
+ *     with the same argument meaning and outputs (csrc/ext.cpp:11-17). A binding that
+ *     today calls the reference's pybind module can call these instead.
+ *
+ *  2. The fused loss path used by fussim_b200.fused_ssim / ssim / SSIM: a forward that
+ *     writes the three SSIM partials and a deterministic in-kernel mean (or per-image
+ *     means) without materialising the SSIM map, and a backward that applies the
+ *     transposed Gaussian with the upstream gradient folded in as a per-image scalar.
+ *
+ * Window sizes 7, 9 and 11 use the reference's Gaussian tables (csrc/ssim.cu:28-64);
+ * the FP16-input entry points use those tables rounded to half precision
+ * (csrc/ssim_fp16.cu:55-82). All arithmetic is FP32.
+ */
+#ifndef FUSSIM_B200_H_
+#define FUSSIM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same layout as cudaStream_t; pass NULL for the legacy default stream. */
+typedef struct CUstream_st* fssim_stream_t;
+
+typedef enum fssim_status {
+  FSSIM_OK = 0,
+  FSSIM_ERR_WINDOW = 1,      /* window_size not in {7, 9, 11} */
+  FSSIM_ERR_SHAPE = 2,       /* a dimension is negative or too large */
+  FSSIM_ERR_DTYPE = 3,       /* unsupported element-type combination */
+  FSSIM_ERR_NULLPTR = 4,     /* a required pointer is NULL */
+  FSSIM_ERR_WORKSPACE = 5,   /* workspace missing or too small */
+  FSSIM_ERR_CUDA = 6,        /* a CUDA runtime call or kernel launch failed */
+  FSSIM_ERR_ARGUMENT = 7     /* any other invalid argument */
+} fssim_status;
+
+typedef enum fssim_dtype {
+  FSSIM_F32 = 0,
+  FSSIM_F16 = 1,
+  FSSIM_BF16 = 2
+} fssim_dtype;
+
+/* Human-readable text for a status code. */
+const char* fssim_status_string(int status);
+
+/* Detail of the last error raised on the calling thread ("" if none). */
+const char* fssim_last_error(void);
+
+/* Library version, e.g. "0.1.0". */
+const char* fssim_version(void);
+
+/* ------------------------------------------------------------------------------------
+ * 1. Reference extension functions (map-producing compat seam)
+ * ------------------------------------------------------------------------------------ */
+
+/* Replaces fusedssim() (csrc/ssim.h:12-20, dispatch csrc/ssim.cu:603-619).
+ * img1/img2: FP32 (B,C,H,W). Writes ssim_map (FP32, B*C*H*W) and, when train != 0, the
+ * three partials dm_dmu1, dm_dsigma1_sq, dm_dsigma12 (FP32, B*C*H*W each; may be NULL
+ * when train == 0). */
+int fssim_fusedssim(int window_size, float C1, float C2, const float* img1, const float* img2,
+                    int64_t B, int64_t C, int64_t H, int64_t W, int train, float* ssim_map,
+                    float* dm_dmu1, float* dm_dsigma1_sq, float* dm_dsigma12,
+                    fssim_stream_t stream);
+
+/* Replaces fusedssim_backward() (csrc/ssim.h:22-33, dispatch csrc/ssim.cu:621-640).
+ * dL_dimg1(p) = sum_q w(q-p) * dL_dmap(q) * [dm_dmu1 + 2 img1(p) dm_dsigma1_sq
+ *                                           + img2(p) dm_dsigma12](q). All FP32. */
+int fssim_fusedssim_backward(int window_size, float C1, float C2, const float* img1,
+                             const float* img2, const float* dL_dmap, const float* dm_dmu1,
+                             const float* dm_dsigma1_sq, const float* dm_dsigma12, int64_t B,
+                             int64_t C, int64_t H, int64_t W, float* dL_dimg1,
+                             fssim_stream_t stream);
+
+/* Replaces fusedssim_fp16() (csrc/ssim_fp16.h:14-20, csrc/ssim_fp16.cu:791-805).
+ * img1/img2: IEEE half bit patterns. Writes the FP32 ssim_map. */
+int fssim_fusedssim_fp16(int window_size, float C1, float C2, const uint16_t* img1,
+                         const uint16_t* img2, int64_t B, int64_t C, int64_t H, int64_t W,
+                         float* ssim_map, fssim_stream_t stream);
+
+/* Replaces fusedssim_fp16_train() (csrc/ssim_fp16.h:22-31, csrc/ssim_fp16.cu:807-822).
+ * Half inputs; FP32 map and FP32 partials. */
+int fssim_fusedssim_fp16_train(int window_size, float C1, float C2, const uint16_t* img1,
+                               const uint16_t* img2, int64_t B, int64_t C, int64_t H,
+                               int64_t W, float* ssim_map, float* dm_dmu1,
+                               float* dm_dsigma1_sq, float* dm_dsigma12,
+                               fssim_stream_t stream);
+
+/* Replaces fusedssim_fp16_backward() (csrc/ssim_fp16.h:33-44, csrc/ssim_fp16.cu:824-842).
+ * Half images; FP32 dL_dmap and partials; FP32 gradient. */
+int fssim_fusedssim_fp16_backward(int window_size, float C1, float C2, const uint16_t* img1,
+                                  const uint16_t* img2, const float* dL_dmap,
+                                  const float* dm_dmu1, const float* dm_dsigma1_sq,
+                                  const float* dm_dsigma12, int64_t B, int64_t C, int64_t H,
+                                  int64_t W, float* dL_dimg1, fssim_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * 2. Fused loss path
+ * ------------------------------------------------------------------------------------ */
+
+typedef enum fssim_reduce {
+  FSSIM_REDUCE_NONE = 0,      /* no reduction outputs */
+  FSSIM_REDUCE_SCALAR = 1,    /* out[0] = out_scale * sum over the whole batch */
+  FSSIM_REDUCE_PER_IMAGE = 2  /* out[b] = out_scale * sum over image b */
+} fssim_reduce;
+
+typedef struct fssim_forward_args {
+  int32_t dtype;          /* fssim_dtype of img1 and img2 (F32 or F16) */
+  int32_t partial_dtype;  /* fssim_dtype of the partials (F32, or F16 with F16 images) */
+  int64_t B, C, H, W;
+  int32_t window_size;    /* 7, 9 or 11 */
+  int32_t valid;          /* 0: 'same' zero padding; 1: 'valid' (border of (w-1)/2 cropped) */
+  int32_t clamp;          /* 1: clamp the map at 0 before reducing (nonnegative_ssim) */
+  int32_t train;          /* 1: write the partials */
+  int32_t reduce;         /* fssim_reduce */
+  float C1, C2;
+  float out_scale;        /* multiplies the reduced sums (e.g. 1/count) */
+  const void* img1;
+  const void* img2;
+  /* Optional per-pixel outputs (NULL to skip): */
+  float* ssim_map;        /* B*C*H*W FP32: the uncropped, unclamped map */
+  void* partials;         /* 3*B*C*H*W of partial_dtype: dm_dmu1 | dm_dsigma1_sq | dm_dsigma12.
+                           * Pre-masked for the fused backward: zero outside the valid
+                           * crop and where the clamp is active. */
+  /* Reduction outputs (required when reduce != NONE): */
+  float* out;             /* 1 (SCALAR) or B (PER_IMAGE) FP32 values */
+  double* image_sums;     /* optional: B FP64 per-image sums of the (cropped, clamped) map */
+  /* Scratch for the reduction: fssim_forward_workspace_bytes(B) bytes, zero-filled before
+   * its first use. Every call leaves it zero-filled again, so it can be reused by later
+   * calls on the same stream; calls that may overlap on the GPU need separate workspaces. */
+  void* workspace;
+  size_t workspace_bytes;
+} fssim_forward_args;
+
+typedef struct fssim_backward_args {
+  int32_t dtype;          /* fssim_dtype of img1/img2 */
+  int32_t partial_dtype;  /* fssim_dtype of the partials */
+  int32_t grad_dtype;     /* fssim_dtype of the gradient written to grad */
+  int64_t B, C, H, W;
+  int32_t window_size;
+  const void* img1;
+  const void* img2;
+  const void* partials;   /* as written by fssim_forward (3*B*C*H*W) */
+  /* dL/dmap(pixel of image b) = chain_scale * grad_out[per_image ? b : 0]
+   * (grad_out == NULL reads as 1). grad_out is an FP32 device pointer. */
+  const float* grad_out;
+  int32_t grad_out_per_image;
+  float chain_scale;
+  void* grad;             /* B*C*H*W of grad_dtype */
+} fssim_backward_args;
+
+/* Bytes of workspace fssim_forward needs for a batch of B images. */
+size_t fssim_forward_workspace_bytes(int64_t B);
+
+/* Fused forward. New in this engine; it replaces the reference's sequence
+ * fusedssim() + valid crop + ssim_map.mean() (fussim/__init__.py:363-369,580). */
+int fssim_forward(const fssim_forward_args* args, fssim_stream_t stream);
+
+/* Fused backward. Replaces the reference's sequence expand(dL/dmean) + valid zero
+ * scatter + fusedssim_backward() (fussim/__init__.py:381-395). */
+int fssim_backward(const fssim_backward_args* args, fssim_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FUSSIM_B200_H_ */
