@@ -447,3 +447,82 @@ int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// fssim_forward_noalloc: the fused forward for callers that cannot allocate GPU memory.
+//
+// fssim_forward needs a small reduction scratch buffer (a ticket word plus one 64-bit
+// accumulator per image) that its caller allocates. Some callers cannot do that: a
+// renderer or game-engine plugin whose host application owns every device allocation and
+// hands the plugin only the buffers it reads and writes, a real-time loop with a fixed
+// memory budget that forbids allocating after start-up, or a binding from a language
+// runtime that has no device allocator at hand. This entry point serves them: its scratch
+// is a fixed array in the library's own device memory, so nothing is allocated per call,
+// by the library or by the caller, who still passes the inputs and outputs.
+//
+// What that costs:
+//  * every GPU that loads this library holds the array (256 B + 8 B per image for
+//    FSSIM_NOALLOC_MAX_IMAGES images, about 33 KiB) until the process exits;
+//  * the array is shared by all calls: two calls whose kernels overlap on the GPU (on
+//    different streams or from different host threads) race on it and return wrong
+//    sums, so such calls must be serialised;
+//  * at most FSSIM_NOALLOC_MAX_IMAGES images per call.
+//
+// The first call on each device looks the array's device address up with
+// cudaGetSymbolAddress (one-time set-up per device); make that first call before any
+// stream capture on that device.
+// ---------------------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes =
+    256 + sizeof(unsigned long long) * static_cast<size_t>(FSSIM_NOALLOC_MAX_IMAGES);
+
+// In host code this name is only a stand-in for the symbol, never a device address: the
+// address handed to the kernel comes from cudaGetSymbolAddress in noalloc_scratch().
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device.
+int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(FSSIM_ERR_CUDA, "device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(FSSIM_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return FSSIM_OK;
+}
+
+}  // namespace
+
+extern "C" int fssim_forward_noalloc(const fssim_forward_args* args, fssim_stream_t stream) {
+  g_last_error.clear();
+  if (!args) return fail(FSSIM_ERR_NULLPTR, "args is NULL");
+  if (args->B > FSSIM_NOALLOC_MAX_IMAGES)
+    return fail(FSSIM_ERR_WORKSPACE,
+                "fssim_forward_noalloc handles at most " + std::to_string(FSSIM_NOALLOC_MAX_IMAGES) +
+                    " images per call, got " + std::to_string(args->B) +
+                    "; use fssim_forward with a caller workspace for larger batches");
+  void* scratch = nullptr;
+  const int st = noalloc_scratch(&scratch);
+  if (st) return st;
+  fssim_forward_args a = *args;
+  a.workspace = scratch;
+  a.workspace_bytes = kNoAllocScratchBytes;
+  if (a.reduce != FSSIM_REDUCE_NONE && a.B > 0) {
+    // The array keeps what the previous call left; the ticket and this call's
+    // accumulators must start at zero.
+    const cudaError_t e =
+        cudaMemsetAsync(scratch, 0, fssim_forward_workspace_bytes(a.B), stream);
+    if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string("clearing scratch: ") + cudaGetErrorString(e));
+  }
+  return fssim_forward(&a, stream);
+}

@@ -170,6 +170,21 @@ int fssim_forward(const fssim_forward_args* args, fssim_stream_t stream);
  * scatter + fusedssim_backward() (fussim/__init__.py:381-395). */
 int fssim_backward(const fssim_backward_args* args, fssim_stream_t stream);
 
+/* Largest batch fssim_forward_noalloc accepts. */
+#define FSSIM_NOALLOC_MAX_IMAGES 4096
+
+/* fssim_forward for callers that cannot allocate GPU memory (no counterpart in the
+ * reference). Same arguments and outputs as fssim_forward; args->workspace and
+ * args->workspace_bytes are ignored. The reduction scratch is a fixed array in the
+ * library's device memory (about 33 KiB, held by every GPU that loads the library until
+ * exit), so nothing is allocated per call: for plugins whose host owns all device memory,
+ * fixed-budget real-time loops, and bindings without a device allocator. Limits: at most
+ * FSSIM_NOALLOC_MAX_IMAGES images (larger B returns FSSIM_ERR_WORKSPACE); all calls share
+ * the array, so calls that overlap on the GPU race and must be serialised; the first call
+ * on each device performs a one-time set-up (cudaGetSymbolAddress) and should come before
+ * any stream capture on that device. */
+int fssim_forward_noalloc(const fssim_forward_args* args, fssim_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
