@@ -39,6 +39,8 @@ int check_shape(int64_t B, int64_t C, int64_t H, int64_t W) {
   if (B < 0 || C < 0 || H < 0 || W < 0) return fail(FSSIM_ERR_SHAPE, "negative dimension");
   if (H > (INT_MAX / 2) || W > (INT_MAX / 2) || C > INT_MAX || B > INT_MAX)
     return fail(FSSIM_ERR_SHAPE, "dimension too large (H, W must be < 2^30)");
+  if (H * W > static_cast<int64_t>(INT_MAX))
+    return fail(FSSIM_ERR_SHAPE, "H*W must be < 2^31 elements per image plane");
   const double n = static_cast<double>(B) * C * H * W;
   if (n > 4.0e18) return fail(FSSIM_ERR_SHAPE, "B*C*H*W overflows int64");
   return FSSIM_OK;
@@ -114,10 +116,10 @@ int launch_error(const char* what) {
   return FSSIM_OK;
 }
 
-template <int HALO, typename TIn, typename TP, bool TRAIN>
+template <int HALO, typename TIn, typename TP, bool TRAIN, bool MERGED>
 int launch_fwd(const fssim::FwdParams& p, cudaStream_t stream) {
-  using Cfg = fssim::FwdConfig<HALO, TIn, TP, TRAIN>;
-  auto k = fssim::ssim_fwd_kernel<HALO, TIn, TP, TRAIN>;
+  using Cfg = fssim::FwdConfig<HALO, TIn, TP, TRAIN, MERGED>;
+  auto k = fssim::ssim_fwd_kernel<HALO, TIn, TP, TRAIN, MERGED>;
   static std::mutex mu;
   static int cache[64] = {0};
   int occ = 0, sms = 0;
@@ -146,12 +148,14 @@ int launch_bwd(const fssim::BwdParams& p, cudaStream_t stream) {
   return launch_error("ssim backward launch");
 }
 
-template <typename TIn, typename TP, bool TRAIN>
+// MERGED selects the fused loss path's 4-map forward; the map-producing reference entry
+// points use the reference's 5 maps.
+template <typename TIn, typename TP, bool TRAIN, bool MERGED>
 int dispatch_fwd(int ws, const fssim::FwdParams& p, cudaStream_t s) {
   switch (ws) {
-    case 7: return launch_fwd<3, TIn, TP, TRAIN>(p, s);
-    case 9: return launch_fwd<4, TIn, TP, TRAIN>(p, s);
-    case 11: return launch_fwd<5, TIn, TP, TRAIN>(p, s);
+    case 7: return launch_fwd<3, TIn, TP, TRAIN, MERGED>(p, s);
+    case 9: return launch_fwd<4, TIn, TP, TRAIN, MERGED>(p, s);
+    case 11: return launch_fwd<5, TIn, TP, TRAIN, MERGED>(p, s);
     default: return fail(FSSIM_ERR_WINDOW, window_message(ws));
   }
 }
@@ -205,8 +209,8 @@ int compat_forward(int ws, float C1, float C2, const TIn* img1, const TIn* img2,
   p.aligned16 = (W % E == 0) && aligned(img1, 16) && aligned(img2, 16);
   p.pair_ok = (W % 2 == 0) && aligned(map, 8) &&
               (!train || (aligned(p0, 8) && aligned(p1, 8) && aligned(p2, 8)));
-  if (train) return dispatch_fwd<TIn, float, true>(ws, p, stream);
-  return dispatch_fwd<TIn, float, false>(ws, p, stream);
+  if (train) return dispatch_fwd<TIn, float, true, false>(ws, p, stream);
+  return dispatch_fwd<TIn, float, false, false>(ws, p, stream);
 }
 
 template <typename TIn>
@@ -393,12 +397,12 @@ int fssim_forward(const fssim_forward_args* a, fssim_stream_t stream) {
   const int ws = a->window_size;
   cudaStream_t s = stream;
   if (a->dtype == FSSIM_F32) {
-    if (a->train) return dispatch_fwd<float, float, true>(ws, p, s);
-    return dispatch_fwd<float, float, false>(ws, p, s);
+    if (a->train) return dispatch_fwd<float, float, true, true>(ws, p, s);
+    return dispatch_fwd<float, float, false, true>(ws, p, s);
   }
-  if (!a->train) return dispatch_fwd<__half, float, false>(ws, p, s);
-  if (a->partial_dtype == FSSIM_F16) return dispatch_fwd<__half, __half, true>(ws, p, s);
-  return dispatch_fwd<__half, float, true>(ws, p, s);
+  if (!a->train) return dispatch_fwd<__half, float, false, true>(ws, p, s);
+  if (a->partial_dtype == FSSIM_F16) return dispatch_fwd<__half, __half, true, true>(ws, p, s);
+  return dispatch_fwd<__half, float, true, true>(ws, p, s);
 }
 
 int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {

@@ -11,7 +11,7 @@
 //   stage   input rows of the step (64 + 16 columns, zero outside the image) -> smem,
 //           issued with cp.async one step ahead so the copy overlaps the previous step;
 //   H-pass  horizontal Gaussian of every staged row -> a smem ring of moment rows
-//           (5 moments forward, 3 chain-weighted partials backward);
+//           (5 moments forward, 3 partials backward);
 //   V-pass  vertical Gaussian of the ring for the step's 32 x 64 outputs, then the
 //           per-pixel epilogue (SSIM + partials, or the gradient).
 //
@@ -20,7 +20,11 @@
 // Zero padding ("same") comes from the zero-filled staging of out-of-image pixels.
 //
 // Arithmetic follows the reference kernels tap for tap (csrc/ssim.cu:200-300,440-503):
-// symmetric taps paired as (left + right) * w for d = 1..HALO, centre last, FP32.
+// symmetric taps paired as (left + right) * w for d = 1..HALO, centre last, FP32, with
+// the squared/cross moments as fma(right, right, left^2). All stencil and epilogue math
+// runs on pairs of adjacent output columns with the sm_100 packed FP32 instructions
+// (fma/add/mul .f32x2), which halve the instruction count at the same FMA throughput and
+// identical per-component rounding.
 //
 // Reduction: each CTA sums its pixels' SSIM per column run (FP32 per thread per step,
 // FP64 across the block), converts the run's sum to 2^-28 fixed point and adds it with
@@ -49,8 +53,10 @@ template <typename T> struct StagePitch;
 template <> struct StagePitch<float> { static constexpr int value = 84; };   // 84 words
 template <> struct StagePitch<__half> { static constexpr int value = 88; };  // 44 words
 
-// Moment-ring pitch in floats: NMAP rows of 64 plus 4 (again 4 * odd words modulo 32).
-template <int NMAP> struct RingPitch { static constexpr int value = NMAP * kStrip + 4; };
+// Moment-ring pitch in floats: NMAP rows of 64 plus 2. The H-pass stores 8-byte column
+// pairs from 32 consecutive rows per warp instruction; a pitch of 2 mod 32 words puts each
+// half warp on 32 distinct banks.
+template <int NMAP> struct RingPitch { static constexpr int value = NMAP * kStrip + 2; };
 
 template <int HALO> struct MaxRows { static constexpr int value = kRows + 2 * HALO; };
 
@@ -78,6 +84,33 @@ template <int HALO, bool HALFW>
 __device__ __forceinline__ float tap(int k) {
   return c_taps[HALFW ? 1 : 0][HALO - 3][k];
 }
+// The packed FMA takes its multiplier as a register pair, not as a constant-bank operand.
+// The HALO+1 distinct taps are therefore loaded once per kernel into register pairs and
+// made opaque to the compiler, so it keeps them live instead of re-materialising a pair
+// from constant memory before every packed FMA.
+template <int HALO, bool HALFW>
+struct Taps2 {
+  float2 w[HALO + 1];  // w[k] = (tap k, tap k), k = 0..HALO (the centre is k = HALO)
+  __device__ __forceinline__ void load() {
+#pragma unroll
+    for (int k = 0; k <= HALO; ++k) {
+      float t = tap<HALO, HALFW>(k);
+      asm volatile("" : "+f"(t));
+      w[k] = make_float2(t, t);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------------------
+// Packed FP32 helpers (per component identical to fmaf / + / *)
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  return __fadd2_rn(a, make_float2(-b.x, -b.y));
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 splat(float v) { return make_float2(v, v); }
 
 // ---------------------------------------------------------------------------------------
 // Small device helpers
@@ -128,109 +161,150 @@ __device__ __forceinline__ void load_vec(const __half* p, float (&v)[NV]) {
   }
 }
 
+// Column pair starting at element s of a loaded row: aligned pairs (s even) come straight
+// from the row, odd starts from the shifted copy.
+template <int NV>
+struct PairRow {
+  float2 a[NV / 2];      // (v[2q], v[2q+1])
+  float2 s[NV / 2 - 1];  // (v[2q+1], v[2q+2])
+  __device__ __forceinline__ void build(const float (&v)[NV]) {
+#pragma unroll
+    for (int q = 0; q < NV / 2; ++q) a[q] = make_float2(v[2 * q], v[2 * q + 1]);
+#pragma unroll
+    for (int q = 0; q < NV / 2 - 1; ++q) s[q] = make_float2(v[2 * q + 1], v[2 * q + 2]);
+  }
+  __device__ __forceinline__ float2 at(int start) const {
+    return (start & 1) ? s[(start - 1) >> 1] : a[start >> 1];
+  }
+};
+
 // Store a pair of adjacent columns (gx, gx+1) of one row; `pair` means both columns are in
 // range and the address is aligned for a vector store.
-__device__ __forceinline__ void store2(float* base, int64_t idx, float a, float b, bool pair,
-                                      bool in0, bool in1) {
+__device__ __forceinline__ void store2(float* base, int64_t idx, float2 v, bool pair, bool in0,
+                                      bool in1) {
   if (pair) {
-    *reinterpret_cast<float2*>(base + idx) = make_float2(a, b);
+    *reinterpret_cast<float2*>(base + idx) = v;
   } else {
-    if (in0) base[idx] = a;
-    if (in1) base[idx + 1] = b;
+    if (in0) base[idx] = v.x;
+    if (in1) base[idx + 1] = v.y;
   }
 }
-__device__ __forceinline__ void store2(__half* base, int64_t idx, float a, float b, bool pair,
-                                      bool in0, bool in1) {
+__device__ __forceinline__ void store2(__half* base, int64_t idx, float2 v, bool pair, bool in0,
+                                      bool in1) {
   if (pair) {
-    *reinterpret_cast<__half2*>(base + idx) = __floats2half2_rn(a, b);
+    *reinterpret_cast<__half2*>(base + idx) = __floats2half2_rn(v.x, v.y);
   } else {
-    if (in0) base[idx] = __float2half_rn(a);
-    if (in1) base[idx + 1] = __float2half_rn(b);
+    if (in0) base[idx] = __float2half_rn(v.x);
+    if (in1) base[idx + 1] = __float2half_rn(v.y);
   }
 }
-__device__ __forceinline__ void store2(__nv_bfloat16* base, int64_t idx, float a, float b,
-                                      bool pair, bool in0, bool in1) {
+__device__ __forceinline__ void store2(__nv_bfloat16* base, int64_t idx, float2 v, bool pair,
+                                      bool in0, bool in1) {
   if (pair) {
-    *reinterpret_cast<__nv_bfloat162*>(base + idx) = __floats2bfloat162_rn(a, b);
+    *reinterpret_cast<__nv_bfloat162*>(base + idx) = __floats2bfloat162_rn(v.x, v.y);
   } else {
-    if (in0) base[idx] = __float2bfloat16_rn(a);
-    if (in1) base[idx + 1] = __float2bfloat16_rn(b);
+    if (in0) base[idx] = __float2bfloat16_rn(v.x);
+    if (in1) base[idx + 1] = __float2bfloat16_rn(v.y);
   }
 }
 
 template <typename T>
-__device__ __forceinline__ void load2(const T* base, int64_t idx, bool pair, bool in0, bool in1,
-                                      float& a, float& b) {
+__device__ __forceinline__ float2 load2(const T* base, int64_t idx, bool pair, bool in0, bool in1) {
   if (pair) {
     if constexpr (sizeof(T) == 4) {
-      const float2 t = *reinterpret_cast<const float2*>(base + idx);
-      a = t.x;
-      b = t.y;
+      return __ldg(reinterpret_cast<const float2*>(base + idx));
     } else {
-      const float2 t = __half22float2(*reinterpret_cast<const __half2*>(base + idx));
-      a = t.x;
-      b = t.y;
+      return __half22float2(__ldg(reinterpret_cast<const __half2*>(base + idx)));
     }
-  } else {
-    a = in0 ? to_f(base[idx]) : 0.f;
-    b = in1 ? to_f(base[idx + 1]) : 0.f;
   }
+  return make_float2(in0 ? to_f(base[idx]) : 0.f, in1 ? to_f(base[idx + 1]) : 0.f);
 }
 
 // ---------------------------------------------------------------------------------------
 // Geometry and step sequencing
 // ---------------------------------------------------------------------------------------
 struct Geometry {
-  int64_t H, W, HW;  // plane geometry
+  int64_t H, W, HW;  // plane geometry (HW < 2^31, checked on the host)
   int64_t LT;        // strip-rows in the whole batch
   int S;             // strips per plane
   int C;             // channels per image
   int B;             // images
 };
 
+// Position of a CTA in its range: the column run (plane, strip) and row of the next step.
+// Advanced incrementally, so a step costs no 64-bit divisions.
 struct Step {
-  int64_t pos;   // linear strip-row index of the first output row of this step
+  int64_t left;   // strip-rows of the CTA's range not yet processed (including this step)
   int64_t plane;
+  int img;        // image of the plane (plane / C), tracked alongside
+  int chan;       // channel of the plane (plane % C)
   int strip;
-  int t;         // first output row (image row index)
-  int n;         // output rows in this step (1..32)
-  int h0;        // first moment row (image row index) computed by this step
-  int nh;        // moment rows computed by this step
-  int hdst;      // ring row receiving moment row h0
-  bool valid;
-  bool last;     // last step of its column run
+  int t;          // first output row of this step
+  int n;          // output rows in this step (1..32); 0 = no step
+  int h0;         // first moment row computed by this step
+  int nh;         // moment rows computed by this step
+  int hdst;       // ring row receiving moment row h0
+  bool last;      // last step of its column run
 };
 
 template <int HALO>
-__device__ __forceinline__ Step make_step(int64_t pos, int64_t beg, int64_t end,
-                                          const Geometry& g) {
-  Step s;
-  s.valid = pos < end;
-  s.pos = pos;
-  if (!s.valid) {
-    s.plane = 0; s.strip = 0; s.t = 0; s.n = 0; s.h0 = 0; s.nh = 0; s.hdst = 0; s.last = true;
-    return s;
-  }
-  const int64_t col = pos / g.H;
-  const int r = static_cast<int>(pos - col * g.H);
-  const int64_t col_end = (col + 1) * g.H;
-  const int64_t run_end = end < col_end ? end : col_end;
-  s.plane = col / g.S;
-  s.strip = static_cast<int>(col - s.plane * g.S);
-  s.t = r;
-  const int64_t left = run_end - pos;
-  s.n = static_cast<int>(left < kRows ? left : kRows);
-  const bool first = (pos == beg) || (r == 0);
-  s.last = (pos + s.n == run_end);
+__device__ __forceinline__ void fill_step(Step& s, bool first, const Geometry& g) {
+  const int rows_left_in_run = static_cast<int>(g.H) - s.t;
+  const int run = s.left < rows_left_in_run ? static_cast<int>(s.left) : rows_left_in_run;
+  s.n = run < kRows ? run : kRows;
+  s.last = (s.n == run);
   if (first) {
-    s.h0 = r - HALO;
+    s.h0 = s.t - HALO;
     s.nh = s.n + 2 * HALO;
     s.hdst = 0;
   } else {
-    s.h0 = r + HALO;
+    s.h0 = s.t + HALO;
     s.nh = s.n;
     s.hdst = 2 * HALO;
   }
+}
+
+template <int HALO>
+__device__ __forceinline__ Step first_step(int64_t beg, int64_t end, const Geometry& g) {
+  Step s;
+  s.left = end - beg;
+  if (s.left <= 0) {
+    s.n = 0;
+    return s;
+  }
+  const int64_t col = beg / g.H;
+  s.t = static_cast<int>(beg - col * g.H);
+  s.plane = col / g.S;
+  s.strip = static_cast<int>(col - s.plane * g.S);
+  s.img = static_cast<int>(s.plane / g.C);
+  s.chan = static_cast<int>(s.plane - static_cast<int64_t>(s.img) * g.C);
+  fill_step<HALO>(s, true, g);
+  return s;
+}
+
+template <int HALO>
+__device__ __forceinline__ Step next_step(const Step& c, const Geometry& g) {
+  Step s = c;
+  s.left = c.left - c.n;
+  if (s.left <= 0) {
+    s.n = 0;
+    return s;
+  }
+  bool first = false;
+  s.t = c.t + c.n;
+  if (s.t == g.H) {  // next column run
+    s.t = 0;
+    first = true;
+    if (++s.strip == g.S) {
+      s.strip = 0;
+      ++s.plane;
+      if (++s.chan == g.C) {
+        s.chan = 0;
+        ++s.img;
+      }
+    }
+  }
+  fill_step<HALO>(s, first, g);
   return s;
 }
 
@@ -241,6 +315,8 @@ __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const 
                                       const Step& s, bool aligned16) {
   constexpr int P = StagePitch<T>::value;
   const int x0 = s.strip * kStrip - kLeft;
+  const int W = static_cast<int>(g.W);
+  const int H = static_cast<int>(g.H);
   if (aligned16) {
     constexpr int E = 16 / sizeof(T);   // elements per 16-byte chunk
     constexpr int CH = kInCols / E;      // chunks per staged row
@@ -254,8 +330,9 @@ __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const 
         const int ch = i - row * CH;
         const int gy = s.h0 + row;
         const int gx = x0 + ch * E;
-        const bool in = (gy >= 0) && (gy < g.H) && (gx >= 0) && (gx < g.W);
-        const T* p = in ? plane + static_cast<int64_t>(gy) * g.W + gx : plane;
+        const bool in = (static_cast<unsigned>(gy) < static_cast<unsigned>(H)) &&
+                        (static_cast<unsigned>(gx) < static_cast<unsigned>(W));
+        const T* p = in ? plane + (gy * W + gx) : plane;
         cp_async16(dst + row * P + ch * E, p, in);
       }
     }
@@ -270,8 +347,9 @@ __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const 
         const int c = i - row * kInCols;
         const int gy = s.h0 + row;
         const int gx = x0 + c;
-        const bool in = (gy >= 0) && (gy < g.H) && (gx >= 0) && (gx < g.W);
-        const T* p = in ? plane + static_cast<int64_t>(gy) * g.W + gx : plane;
+        const bool in = (static_cast<unsigned>(gy) < static_cast<unsigned>(H)) &&
+                        (static_cast<unsigned>(gx) < static_cast<unsigned>(W));
+        const T* p = in ? plane + (gy * W + gx) : plane;
         cp_async4(dst + row * P + c, p, in);
       }
     }
@@ -287,24 +365,24 @@ __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const 
         const int c = i - row * kInCols;
         const int gy = s.h0 + row;
         const int gx = x0 + c;
-        const bool in = (gy >= 0) && (gy < g.H) && (gx >= 0) && (gx < g.W);
-        dst[row * P + c] = in ? plane[static_cast<int64_t>(gy) * g.W + gx] : T(0.f);
+        const bool in = (static_cast<unsigned>(gy) < static_cast<unsigned>(H)) &&
+                        (static_cast<unsigned>(gx) < static_cast<unsigned>(W));
+        dst[row * P + c] = in ? plane[gy * W + gx] : T(0.f);
       }
     }
   }
   cp_async_commit();
 }
 
-// Copy ring rows [n, n + 2*HALO) to [0, 2*HALO): the vertical halo for the next step.
+// Copy ring rows [32, 32 + 2*HALO) to [0, 2*HALO): the vertical halo for the next step.
+// Only full 32-row steps carry, so source and destination are disjoint contiguous blocks.
 template <int HALO, int RP>
-__device__ __forceinline__ void ring_carry(float* ring, int n) {
-  constexpr int V = RP / 4;  // float4 per ring row
-  float4* r4 = reinterpret_cast<float4*>(ring);
-  for (int i = threadIdx.x; i < 2 * HALO * V; i += kThreads) {
-    const int row = i / V;
-    const int c = i - row * V;
-    r4[row * V + c] = r4[(n + row) * V + c];
-  }
+__device__ __forceinline__ void ring_carry(float* ring) {
+  static_assert((2 * HALO * RP) % 4 == 0 && (kRows * RP) % 4 == 0, "float4 carry");
+  constexpr int N4 = 2 * HALO * RP / 4;
+  const float4* src = reinterpret_cast<const float4*>(ring + kRows * RP);
+  float4* dst = reinterpret_cast<float4*>(ring);
+  for (int i = threadIdx.x; i < N4; i += kThreads) dst[i] = src[i];
 }
 
 // Deterministic block sum of a double (fixed shuffle tree, warps combined in order).
@@ -316,6 +394,21 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
   if (lane == 0) red[warp] = v;
   __syncthreads();
   return ((red[0] + red[1]) + red[2]) + red[3];
+}
+
+// Vertical 2*HALO+1 tap sum of column pairs for 8 consecutive output rows: rows k..k+2HALO
+// of `v` feed output k (reference order: pairs d = 1..HALO, centre last).
+template <int HALO, bool HW_>
+__device__ __forceinline__ void vsum8(const float2 (&v)[8 + 2 * HALO], float2 (&o)[8],
+                                      const Taps2<HALO, HW_>& T) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int d = 1; d <= HALO; ++d)
+      acc = fma2(add2(v[k + HALO - d], v[k + HALO + d]), T.w[HALO - d], acc);
+    o[k] = fma2(v[k + HALO], T.w[HALO], acc);
+  }
 }
 
 // ---------------------------------------------------------------------------------------
@@ -337,82 +430,116 @@ struct FwdParams {
   int valid, clamp, reduce, mask_partials, aligned16, pair_ok;
 };
 
-template <int HALO, typename TIn, typename TP, bool TRAIN>
+// MERGED (the fused loss path): the SSIM value and its partials depend on the second moments
+// only through sigma1^2 + sigma2^2 (in B), so one map E[x^2 + y^2] replaces E[x^2] and
+// E[y^2]: 4 filtered maps instead of 5. Its FP32 rounding error against an exact result is
+// the same size as that of the separate maps (both are dominated by the cancellation in
+// E[.] - mu^2). The map-producing reference entry points keep the reference's 5 maps
+// (MERGED = false) so their per-pixel outputs follow its arithmetic order exactly.
+template <int HALO, typename TIn, typename TP, bool TRAIN, bool MERGED>
 struct FwdConfig {
   static constexpr bool kHalfW = sizeof(TIn) == 2;
+  static constexpr int kMaps = MERGED ? 4 : 5;
   static constexpr int kMaxR = MaxRows<HALO>::value;
   static constexpr int kSP = StagePitch<TIn>::value;
-  static constexpr int kRP = RingPitch<5>::value;
+  static constexpr int kRP = RingPitch<kMaps>::value;
   static constexpr size_t kStageBytes = 2ull * kMaxR * kSP * sizeof(TIn);
   static constexpr size_t kRingBytes = static_cast<size_t>(kMaxR) * kRP * sizeof(float);
   static constexpr size_t kSmem = kStageBytes + kRingBytes;
+  // resident CTAs per SM the kernel is compiled for (228 KB of shared memory per SM)
+  static constexpr int kMinBlocks = (kSmem + 1024) * 3 <= 228 * 1024 ? 3 : 2;
 };
 
 // Horizontal pass of the forward: for staged row i and output columns 8j..8j+7 compute the
-// five moments sum w*X, w*X^2, w*Y, w*Y^2, w*XY (order of the reference's xconv features).
-template <int HALO, typename TIn, int MAXR>
+// moments sum w*X, w*X^2, w*Y, w*Y^2, w*XY (order of the reference's xconv features), or
+// with MERGED sum w*X, w*(X^2+Y^2), w*Y, w*XY, as four column pairs.
+template <int HALO, typename TIn, int MAXR, bool MERGED>
 __device__ __forceinline__ void fwd_hpass(const TIn* sx, const TIn* sy, float* ring, int nh,
-                                          int hdst) {
-  constexpr bool HW_ = sizeof(TIn) == 2;
+                                          int hdst, const Taps2<HALO, sizeof(TIn) == 2>& T) {
   constexpr int SP = StagePitch<TIn>::value;
-  constexpr int RP = RingPitch<5>::value;
+  constexpr int RP = RingPitch<MERGED ? 4 : 5>::value;
   constexpr int HA = (sizeof(TIn) == 2 || HALO > 4) ? 8 : 4;  // aligned left extent
   constexpr int NV = 8 + 2 * HA;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int rg = 0; rg < nh; rg += 32) {
     const int i = rg + lane;
     if (i < nh) {
-#pragma unroll
+#pragma unroll 1
       for (int jj = 0; jj < 2; ++jj) {
         const int j = warp + 4 * jj;
         float xv[NV], yv[NV];
         load_vec(sx + i * SP + 8 * j + kLeft - HA, xv);
         load_vec(sy + i * SP + 8 * j + kLeft - HA, yv);
-        float xx[NV], yy[NV], xy[NV];
+        PairRow<NV> X, Y, XX, YY, XY;
+        X.build(xv);
+        Y.build(yv);
 #pragma unroll
-        for (int q = HA - HALO; q < HA + 8; ++q) {
-          xx[q] = xv[q] * xv[q];
-          yy[q] = yv[q] * yv[q];
-          xy[q] = xv[q] * yv[q];
+        for (int q = 0; q < NV / 2; ++q) {
+          XX.a[q] = mul2(X.a[q], X.a[q]);
+          XY.a[q] = mul2(X.a[q], Y.a[q]);
+          YY.a[q] = MERGED ? fma2(Y.a[q], Y.a[q], XX.a[q]) : mul2(Y.a[q], Y.a[q]);
         }
-        float o[5][8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int c = HA + k;
-          float sX = 0.f, sX2 = 0.f, sY = 0.f, sY2 = 0.f, sXY = 0.f;
-#pragma unroll
-          for (int d = 1; d <= HALO; ++d) {
-            const float w = tap<HALO, HW_>(HALO - d);
-            const int l = c - d, r = c + d;
-            sX = fmaf(xv[l] + xv[r], w, sX);
-            sX2 = fmaf(fmaf(xv[r], xv[r], xx[l]), w, sX2);
-            sY = fmaf(yv[l] + yv[r], w, sY);
-            sY2 = fmaf(fmaf(yv[r], yv[r], yy[l]), w, sY2);
-            sXY = fmaf(fmaf(xv[r], yv[r], xy[l]), w, sXY);
-          }
-          const float wc = tap<HALO, HW_>(HALO);
-          o[0][k] = fmaf(xv[c], wc, sX);
-          o[1][k] = fmaf(xx[c], wc, sX2);
-          o[2][k] = fmaf(yv[c], wc, sY);
-          o[3][k] = fmaf(yy[c], wc, sY2);
-          o[4][k] = fmaf(xy[c], wc, sXY);
+        for (int q = 0; q < NV / 2 - 1; ++q) {
+          XX.s[q] = mul2(X.s[q], X.s[q]);
+          XY.s[q] = mul2(X.s[q], Y.s[q]);
+          YY.s[q] = MERGED ? fma2(Y.s[q], Y.s[q], XX.s[q]) : mul2(Y.s[q], Y.s[q]);
         }
         float* dst = ring + (hdst + i) * RP + 8 * j;
+        if constexpr (MERGED) {
+          // YY holds x^2 + y^2; ring maps: 0 = X, 1 = X^2+Y^2, 2 = Y, 3 = XY
 #pragma unroll
-        for (int m = 0; m < 5; ++m) {
-          reinterpret_cast<float4*>(dst + m * kStrip)[0] =
-              make_float4(o[m][0], o[m][1], o[m][2], o[m][3]);
-          reinterpret_cast<float4*>(dst + m * kStrip)[1] =
-              make_float4(o[m][4], o[m][5], o[m][6], o[m][7]);
+          for (int p = 0; p < 4; ++p) {
+            const int c = HA + 2 * p;
+            float2 sX = make_float2(0.f, 0.f), sS = sX, sY = sX, sXY = sX;
+#pragma unroll
+            for (int d = 1; d <= HALO; ++d) {
+              const float2 w = T.w[HALO - d];
+              const int l = c - d, r = c + d;
+              sX = fma2(add2(X.at(l), X.at(r)), w, sX);
+              sS = fma2(add2(YY.at(l), YY.at(r)), w, sS);
+              sY = fma2(add2(Y.at(l), Y.at(r)), w, sY);
+              sXY = fma2(fma2(X.at(r), Y.at(r), XY.at(l)), w, sXY);
+            }
+            const float2 wc = T.w[HALO];
+            *reinterpret_cast<float2*>(dst + 0 * kStrip + 2 * p) = fma2(X.at(c), wc, sX);
+            *reinterpret_cast<float2*>(dst + 1 * kStrip + 2 * p) = fma2(YY.at(c), wc, sS);
+            *reinterpret_cast<float2*>(dst + 2 * kStrip + 2 * p) = fma2(Y.at(c), wc, sY);
+            *reinterpret_cast<float2*>(dst + 3 * kStrip + 2 * p) = fma2(XY.at(c), wc, sXY);
+          }
+          continue;
+        }
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const int c = HA + 2 * p;  // first column of the output pair
+          float2 sX = make_float2(0.f, 0.f), sX2 = sX, sY = sX, sY2 = sX, sXY = sX;
+#pragma unroll
+          for (int d = 1; d <= HALO; ++d) {
+            const float2 w = T.w[HALO - d];
+            const int l = c - d, r = c + d;
+            sX = fma2(add2(X.at(l), X.at(r)), w, sX);
+            sX2 = fma2(fma2(X.at(r), X.at(r), XX.at(l)), w, sX2);
+            sY = fma2(add2(Y.at(l), Y.at(r)), w, sY);
+            sY2 = fma2(fma2(Y.at(r), Y.at(r), YY.at(l)), w, sY2);
+            sXY = fma2(fma2(X.at(r), Y.at(r), XY.at(l)), w, sXY);
+          }
+          const float2 wc = T.w[HALO];
+          *reinterpret_cast<float2*>(dst + 0 * kStrip + 2 * p) = fma2(X.at(c), wc, sX);
+          *reinterpret_cast<float2*>(dst + 1 * kStrip + 2 * p) = fma2(XX.at(c), wc, sX2);
+          *reinterpret_cast<float2*>(dst + 2 * kStrip + 2 * p) = fma2(Y.at(c), wc, sY);
+          *reinterpret_cast<float2*>(dst + 3 * kStrip + 2 * p) = fma2(YY.at(c), wc, sY2);
+          *reinterpret_cast<float2*>(dst + 4 * kStrip + 2 * p) = fma2(XY.at(c), wc, sXY);
         }
       }
     }
   }
 }
 
-template <int HALO, typename TIn, typename TP, bool TRAIN>
-__global__ void __launch_bounds__(kThreads, 2) ssim_fwd_kernel(const FwdParams a) {
-  using Cfg = FwdConfig<HALO, TIn, TP, TRAIN>;
+template <int HALO, typename TIn, typename TP, bool TRAIN, bool MERGED>
+__global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MERGED>::kMinBlocks))
+    ssim_fwd_kernel(const FwdParams a) {
+  using Cfg = FwdConfig<HALO, TIn, TP, TRAIN, MERGED>;
+  constexpr int NM = Cfg::kMaps;
   constexpr int MAXR = Cfg::kMaxR;
   constexpr int SP = Cfg::kSP;
   constexpr int RP = Cfg::kRP;
@@ -429,45 +556,40 @@ __global__ void __launch_bounds__(kThreads, 2) ssim_fwd_kernel(const FwdParams a
   const TIn* const src[2] = {static_cast<const TIn*>(a.img1), static_cast<const TIn*>(a.img2)};
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r0 = warp * 8;
+  const float2 C1v = splat(a.C1), C2v = splat(a.C2), two = splat(2.f);
+  Taps2<HALO, HW_> T;
+  T.load();
 
-  Step cur = make_step<HALO>(beg, beg, end, g);
-  if (cur.valid) stage<TIn, 2, MAXR>(stg, src, g, cur, a.aligned16);
+  Step cur = first_step<HALO>(beg, end, g);
+  if (cur.n) stage<TIn, 2, MAXR>(stg, src, g, cur, a.aligned16);
   double run_sum = 0.0;
 
-  while (cur.valid) {
+  while (cur.n) {
     cp_async_wait_all();
     __syncthreads();
-    fwd_hpass<HALO, TIn, MAXR>(stg, stg + MAXR * SP, ring, cur.nh, cur.hdst);
+    fwd_hpass<HALO, TIn, MAXR, MERGED>(stg, stg + MAXR * SP, ring, cur.nh, cur.hdst, T);
     __syncthreads();
-    const Step nxt = make_step<HALO>(cur.pos + cur.n, beg, end, g);
-    if (nxt.valid) stage<TIn, 2, MAXR>(stg, src, g, nxt, a.aligned16);
+    const Step nxt = next_step<HALO>(cur, g);
+    if (nxt.n) stage<TIn, 2, MAXR>(stg, src, g, nxt, a.aligned16);
 
     // ---- V-pass + epilogue: rows r0..r0+7 of the step, columns 2*lane, 2*lane+1 ----
     if (r0 < cur.n) {
-      float res[5][8][2];
+      float2 res[NM][8];
 #pragma unroll
-      for (int m = 0; m < 5; ++m) {
+      for (int m = 0; m < NM; ++m) {
         float2 v[8 + 2 * HALO];
 #pragma unroll
         for (int q = 0; q < 8 + 2 * HALO; ++q)
           v[q] = *reinterpret_cast<const float2*>(ring + (r0 + q) * RP + m * kStrip + 2 * lane);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          float ox = 0.f, oy = 0.f;
-#pragma unroll
-          for (int d = 1; d <= HALO; ++d) {
-            const float w = tap<HALO, HW_>(HALO - d);
-            ox = fmaf(v[k + HALO - d].x + v[k + HALO + d].x, w, ox);
-            oy = fmaf(v[k + HALO - d].y + v[k + HALO + d].y, w, oy);
-          }
-          const float wc = tap<HALO, HW_>(HALO);
-          res[m][k][0] = fmaf(v[k + HALO].x, wc, ox);
-          res[m][k][1] = fmaf(v[k + HALO].y, wc, oy);
-        }
+        vsum8<HALO, HW_>(v, res[m], T);
       }
       const int gx0 = cur.strip * kStrip + 2 * lane;
-      const bool in0 = gx0 < g.W, in1 = gx0 + 1 < g.W;
+      const int W = static_cast<int>(g.W);
+      const bool in0 = gx0 < W, in1 = gx0 + 1 < W;
       const bool pair = a.pair_ok && in1;
+      // columns counted in the reduction / receiving gradient (valid crop)
+      const bool col0 = in0 && (!a.valid || (gx0 >= HALO && gx0 < W - HALO));
+      const bool col1 = in1 && (!a.valid || (gx0 + 1 >= HALO && gx0 + 1 < W - HALO));
       const int64_t plane_off = cur.plane * g.HW;
       float step_sum = 0.f;
 #pragma unroll
@@ -476,41 +598,46 @@ __global__ void __launch_bounds__(kThreads, 2) ssim_fwd_kernel(const FwdParams a
         if (row < cur.n) {
           const int gy = cur.t + row;
           const bool row_ok = !a.valid || (gy >= HALO && gy < g.H - HALO);
-          float val[2], pm[2], ps[2], pc[2];
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const float mu1 = res[0][k][c], mu2 = res[2][k][c];
-            const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2;
-            const float sigma1_sq = res[1][k][c] - mu1_sq;
-            const float sigma2_sq = res[3][k][c] - mu2_sq;
-            const float sigma12 = res[4][k][c] - mu1 * mu2;
-            const float A = mu1_sq + mu2_sq + a.C1;
-            const float B = sigma1_sq + sigma2_sq + a.C2;
-            const float Cc = 2.f * mu1 * mu2 + a.C1;
-            const float D = 2.f * sigma12 + a.C2;
-            const float rA = __fdividef(1.f, A);
-            const float rB = __fdividef(1.f, B);
-            const float rAB = rA * rB;
-            const float v = (Cc * D) * rAB;
-            val[c] = v;
-            const int gx = gx0 + c;
-            const bool in = c == 0 ? in0 : in1;
-            const bool counted =
-                in && row_ok && (!a.valid || (gx >= HALO && gx < g.W - HALO));
-            if (a.reduce && counted) step_sum += (a.clamp && v < 0.f) ? 0.f : v;
-            if (TRAIN) {
-              const bool live = !a.mask_partials || (counted && (!a.clamp || v >= 0.f));
-              pm[c] = live ? 2.f * mu2 * (D - Cc) * rAB + 2.f * mu1 * v * (rB - rA) : 0.f;
-              ps[c] = live ? -v * rB : 0.f;
-              pc[c] = live ? 2.f * Cc * rAB : 0.f;
-            }
+          const float2 mu1 = res[0][k], mu2 = res[2][k];
+          const float2 mu1_sq = mul2(mu1, mu1), mu2_sq = mul2(mu2, mu2);
+          const float2 msq = add2(mu1_sq, mu2_sq);
+          const float2 A = add2(msq, C1v);
+          float2 B, sigma12;
+          if constexpr (MERGED) {
+            B = add2(sub2(res[1][k], msq), C2v);
+            sigma12 = sub2(res[3][k], mul2(mu1, mu2));
+          } else {
+            const float2 sigma1_sq = sub2(res[1][k], mu1_sq);
+            const float2 sigma2_sq = sub2(res[3][k], mu2_sq);
+            B = add2(add2(sigma1_sq, sigma2_sq), C2v);
+            sigma12 = sub2(res[NM - 1][k], mul2(mu1, mu2));
+          }
+          const float2 Cc = fma2(mul2(two, mu1), mu2, C1v);
+          const float2 D = fma2(two, sigma12, C2v);
+          const float2 rA = make_float2(__fdividef(1.f, A.x), __fdividef(1.f, A.y));
+          const float2 rB = make_float2(__fdividef(1.f, B.x), __fdividef(1.f, B.y));
+          const float2 rAB = mul2(rA, rB);
+          const float2 v = mul2(mul2(Cc, D), rAB);
+          const bool c0 = row_ok && col0, c1 = row_ok && col1;
+          if (a.reduce) {
+            const float v0 = (a.clamp && v.x < 0.f) ? 0.f : v.x;
+            const float v1 = (a.clamp && v.y < 0.f) ? 0.f : v.y;
+            step_sum += (c0 ? v0 : 0.f) + (c1 ? v1 : 0.f);
           }
           const int64_t idx = plane_off + static_cast<int64_t>(gy) * g.W + gx0;
-          if (a.map) store2(a.map, idx, val[0], val[1], pair, in0, in1);
+          if (a.map) store2(a.map, idx, v, pair, in0, in1);
           if (TRAIN) {
-            store2(static_cast<TP*>(a.p0), idx, pm[0], pm[1], pair, in0, in1);
-            store2(static_cast<TP*>(a.p1), idx, ps[0], ps[1], pair, in0, in1);
-            store2(static_cast<TP*>(a.p2), idx, pc[0], pc[1], pair, in0, in1);
+            const bool live0 = !a.mask_partials || (c0 && (!a.clamp || v.x >= 0.f));
+            const bool live1 = !a.mask_partials || (c1 && (!a.clamp || v.y >= 0.f));
+            float2 pm = fma2(mul2(two, mu2), mul2(sub2(D, Cc), rAB),
+                             mul2(mul2(two, mu1), mul2(v, sub2(rB, rA))));
+            float2 ps = mul2(make_float2(-v.x, -v.y), rB);
+            float2 pc = mul2(mul2(two, Cc), rAB);
+            if (!live0) pm.x = ps.x = pc.x = 0.f;
+            if (!live1) pm.y = ps.y = pc.y = 0.f;
+            store2(static_cast<TP*>(a.p0), idx, pm, pair, in0, in1);
+            store2(static_cast<TP*>(a.p1), idx, ps, pair, in0, in1);
+            store2(static_cast<TP*>(a.p2), idx, pc, pair, in0, in1);
           }
         }
       }
@@ -522,15 +649,12 @@ __global__ void __launch_bounds__(kThreads, 2) ssim_fwd_kernel(const FwdParams a
       const double s = block_sum(run_sum, red);
       run_sum = 0.0;
       if (threadIdx.x == 0) {
-        const int64_t b = cur.plane / g.C;
         const long long q = __double2ll_rn(s * kFixScale);
-        atomicAdd(a.acc + b, static_cast<unsigned long long>(q));
+        atomicAdd(a.acc + cur.img, static_cast<unsigned long long>(q));
       }
     }
     __syncthreads();
-    if (!cur.last) {
-      ring_carry<HALO, RP>(ring, cur.n);
-    }
+    if (!cur.last) ring_carry<HALO, RP>(ring);
     cur = nxt;
   }
 
@@ -586,55 +710,50 @@ struct BwdConfig {
       DLMAP ? static_cast<size_t>(kMaxR) * StagePitch<float>::value * sizeof(float) : 0;
   static constexpr size_t kRingBytes = static_cast<size_t>(kMaxR) * kRP * sizeof(float);
   static constexpr size_t kSmem = kStageBytes + kDlBytes + kRingBytes;
+  static constexpr int kMinBlocks = (kSmem + 1024) * 3 <= 228 * 1024 ? 3 : 2;
 };
 
 // Horizontal pass of the backward over the three partial maps (times dL/dmap on the
 // general path, as the reference multiplies at load, csrc/ssim.cu:408-411).
 template <int HALO, typename TIn, typename TP, bool DLMAP, int MAXR>
 __device__ __forceinline__ void bwd_hpass(const TP* sp, const float* sdl, float* ring, int nh,
-                                          int hdst) {
-  constexpr bool HW_ = sizeof(TIn) == 2;
+                                          int hdst, const Taps2<HALO, sizeof(TIn) == 2>& T) {
   constexpr int SP = StagePitch<TP>::value;
   constexpr int RP = RingPitch<3>::value;
   constexpr int HA = (sizeof(TP) == 2 || HALO > 4) ? 8 : 4;
   constexpr int NV = 8 + 2 * HA;
+  // The general path only exists for FP32 partials, so dL and the partials share the
+  // staged layout (same pitch, same aligned left extent HA).
+  static_assert(!DLMAP || sizeof(TP) == 4, "per-pixel dL/dmap needs FP32 partials");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int rg = 0; rg < nh; rg += 32) {
     const int i = rg + lane;
     if (i < nh) {
-#pragma unroll
+#pragma unroll 1
       for (int jj = 0; jj < 2; ++jj) {
         const int j = warp + 4 * jj;
-        // The general path only exists for FP32 partials, so dL and the partials share
-        // the staged layout (pitch 84, same aligned left extent HA).
-        static_assert(!DLMAP || sizeof(TP) == 4, "per-pixel dL/dmap needs FP32 partials");
         float dl[NV];
         if (DLMAP) load_vec(sdl + i * StagePitch<float>::value + 8 * j + kLeft - HA, dl);
-        float o[3][8];
+        float* dst = ring + (hdst + i) * RP + 8 * j;
 #pragma unroll
         for (int m = 0; m < 3; ++m) {
           float v[NV];
           load_vec(sp + (m * MAXR + i) * SP + 8 * j + kLeft - HA, v);
           if (DLMAP) {
 #pragma unroll
-            for (int q = HA - HALO; q < HA + 8 + HALO; ++q) v[q] = v[q] * dl[q];
+            for (int q = 0; q < NV; ++q) v[q] = v[q] * dl[q];
           }
+          PairRow<NV> V;
+          V.build(v);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int c = HA + k;
-            float s = 0.f;
+          for (int p = 0; p < 4; ++p) {
+            const int c = HA + 2 * p;
+            float2 s = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int d = 1; d <= HALO; ++d) s = fmaf(v[c - d] + v[c + d], tap<HALO, HW_>(HALO - d), s);
-            o[m][k] = fmaf(v[c], tap<HALO, HW_>(HALO), s);
+            for (int d = 1; d <= HALO; ++d)
+              s = fma2(add2(V.at(c - d), V.at(c + d)), T.w[HALO - d], s);
+            *reinterpret_cast<float2*>(dst + m * kStrip + 2 * p) = fma2(V.at(c), T.w[HALO], s);
           }
-        }
-        float* dst = ring + (hdst + i) * RP + 8 * j;
-#pragma unroll
-        for (int m = 0; m < 3; ++m) {
-          reinterpret_cast<float4*>(dst + m * kStrip)[0] =
-              make_float4(o[m][0], o[m][1], o[m][2], o[m][3]);
-          reinterpret_cast<float4*>(dst + m * kStrip)[1] =
-              make_float4(o[m][4], o[m][5], o[m][6], o[m][7]);
         }
       }
     }
@@ -642,7 +761,8 @@ __device__ __forceinline__ void bwd_hpass(const TP* sp, const float* sdl, float*
 }
 
 template <int HALO, typename TIn, typename TP, bool DLMAP>
-__global__ void __launch_bounds__(kThreads, 2) ssim_bwd_kernel(const BwdParams a) {
+__global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kMinBlocks))
+    ssim_bwd_kernel(const BwdParams a) {
   using Cfg = BwdConfig<HALO, TIn, TP, DLMAP>;
   constexpr int MAXR = Cfg::kMaxR;
   constexpr int RP = Cfg::kRP;
@@ -662,80 +782,77 @@ __global__ void __launch_bounds__(kThreads, 2) ssim_bwd_kernel(const BwdParams a
   const TIn* img2 = static_cast<const TIn*>(a.img2);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r0 = warp * 8;
+  const float2 two = splat(2.f);
+  Taps2<HALO, HW_> T;
+  T.load();
 
-  Step cur = make_step<HALO>(beg, beg, end, g);
-  if (cur.valid) {
+  Step cur = first_step<HALO>(beg, end, g);
+  if (cur.n) {
     stage<TP, 3, MAXR>(stg, src, g, cur, a.aligned16);
     if (DLMAP) stage<float, 1, MAXR>(sdl, dsrc, g, cur, a.aligned16);
   }
-  while (cur.valid) {
+  while (cur.n) {
     cp_async_wait_all();
     __syncthreads();
-    bwd_hpass<HALO, TIn, TP, DLMAP, MAXR>(stg, sdl, ring, cur.nh, cur.hdst);
+    bwd_hpass<HALO, TIn, TP, DLMAP, MAXR>(stg, sdl, ring, cur.nh, cur.hdst, T);
     __syncthreads();
-    const Step nxt = make_step<HALO>(cur.pos + cur.n, beg, end, g);
-    if (nxt.valid) {
+    const Step nxt = next_step<HALO>(cur, g);
+    if (nxt.n) {
       stage<TP, 3, MAXR>(stg, src, g, nxt, a.aligned16);
       if (DLMAP) stage<float, 1, MAXR>(sdl, dsrc, g, nxt, a.aligned16);
     }
 
     if (r0 < cur.n) {
       const int gx0 = cur.strip * kStrip + 2 * lane;
-      const bool in0 = gx0 < g.W, in1 = gx0 + 1 < g.W;
+      const int W = static_cast<int>(g.W);
+      const bool in0 = gx0 < W, in1 = gx0 + 1 < W;
       const bool pair = a.pair_ok && in1;
       const int64_t plane_off = cur.plane * g.HW;
-      float chain = a.chain_scale;
-      if (!DLMAP && a.grad_out) {
-        const int64_t b = cur.plane / g.C;
-        chain *= a.grad_out[a.grad_per_image ? b : 0];
+      // Issue the epilogue's image loads before the vertical pass so they are in flight
+      // while it runs.
+      const int64_t row_base = plane_off + static_cast<int64_t>(cur.t + r0) * g.W + gx0;
+      float2 xin[8], yin[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        xin[k] = make_float2(0.f, 0.f);
+        yin[k] = xin[k];
+        if (r0 + k < cur.n) {
+          const int64_t idx = row_base + k * g.W;
+          xin[k] = load2(img1, idx, pair, in0, in1);
+          yin[k] = load2(img2, idx, pair, in0, in1);
+        }
       }
-      float res[3][8][2];
+      float2 chain = splat(a.chain_scale);
+      if (!DLMAP && a.grad_out) {
+        chain = mul2(chain, splat(a.grad_out[a.grad_per_image ? cur.img : 0]));
+      }
+      float2 res[3][8];
 #pragma unroll
       for (int m = 0; m < 3; ++m) {
         float2 v[8 + 2 * HALO];
 #pragma unroll
         for (int q = 0; q < 8 + 2 * HALO; ++q)
           v[q] = *reinterpret_cast<const float2*>(ring + (r0 + q) * RP + m * kStrip + 2 * lane);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          float ox = 0.f, oy = 0.f;
-#pragma unroll
-          for (int d = 1; d <= HALO; ++d) {
-            const float w = tap<HALO, HW_>(HALO - d);
-            ox = fmaf(v[k + HALO - d].x + v[k + HALO + d].x, w, ox);
-            oy = fmaf(v[k + HALO - d].y + v[k + HALO + d].y, w, oy);
-          }
-          const float wc = tap<HALO, HW_>(HALO);
-          res[m][k][0] = fmaf(v[k + HALO].x, wc, ox);
-          res[m][k][1] = fmaf(v[k + HALO].y, wc, oy);
-        }
+        vsum8<HALO, HW_>(v, res[m], T);
       }
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int row = r0 + k;
         if (row < cur.n) {
-          const int gy = cur.t + row;
-          const int64_t idx = plane_off + static_cast<int64_t>(gy) * g.W + gx0;
-          float x0v, x1v, y0v, y1v;
-          load2(img1, idx, pair, in0, in1, x0v, x1v);
-          load2(img2, idx, pair, in0, in1, y0v, y1v);
-          float gv0 = fmaf(y0v, res[2][k][0], fmaf(2.f * x0v, res[1][k][0], res[0][k][0]));
-          float gv1 = fmaf(y1v, res[2][k][1], fmaf(2.f * x1v, res[1][k][1], res[0][k][1]));
-          if (!DLMAP) {
-            gv0 *= chain;
-            gv1 *= chain;
-          }
+          const int64_t idx = row_base + k * g.W;
+          float2 gv = fma2(yin[k], res[2][k], fma2(mul2(two, xin[k]), res[1][k], res[0][k]));
+          if (!DLMAP) gv = mul2(gv, chain);
           if (a.grad_dtype == 0)
-            store2(static_cast<float*>(a.grad), idx, gv0, gv1, pair, in0, in1);
+            store2(static_cast<float*>(a.grad), idx, gv, pair, in0, in1);
           else if (a.grad_dtype == 1)
-            store2(static_cast<__half*>(a.grad), idx, gv0, gv1, pair, in0, in1);
+            store2(static_cast<__half*>(a.grad), idx, gv, pair, in0, in1);
           else
-            store2(static_cast<__nv_bfloat16*>(a.grad), idx, gv0, gv1, pair, in0, in1);
+            store2(static_cast<__nv_bfloat16*>(a.grad), idx, gv, pair, in0, in1);
         }
       }
     }
     __syncthreads();
-    if (!cur.last) ring_carry<HALO, RP>(ring, cur.n);
+    if (!cur.last) ring_carry<HALO, RP>(ring);
     cur = nxt;
   }
 }
