@@ -161,22 +161,38 @@ __device__ __forceinline__ void load_vec(const __half* p, float (&v)[NV]) {
   }
 }
 
-// Column pair starting at element s of a loaded row: aligned pairs (s even) come straight
-// from the row, odd starts from the shifted copy.
+// A loaded row held as aligned column pairs (v[2q], v[2q+1]). Packed operands that start
+// at an even column are these pairs. Odd-start pairs are never built: the compiler would
+// re-assemble them with register moves at every use. Instead odd taps combine single
+// elements with scalar instructions that write the two halves of a result pair directly.
 template <int NV>
 struct PairRow {
-  float2 a[NV / 2];      // (v[2q], v[2q+1])
-  float2 s[NV / 2 - 1];  // (v[2q+1], v[2q+2])
+  float2 a[NV / 2];
   __device__ __forceinline__ void build(const float (&v)[NV]) {
 #pragma unroll
     for (int q = 0; q < NV / 2; ++q) a[q] = make_float2(v[2 * q], v[2 * q + 1]);
-#pragma unroll
-    for (int q = 0; q < NV / 2 - 1; ++q) s[q] = make_float2(v[2 * q + 1], v[2 * q + 2]);
   }
-  __device__ __forceinline__ float2 at(int start) const {
-    return (start & 1) ? s[(start - 1) >> 1] : a[start >> 1];
-  }
+  __device__ __forceinline__ float el(int i) const { return (i & 1) ? a[i >> 1].y : a[i >> 1].x; }
+  __device__ __forceinline__ float2 pr(int i) const { return a[i >> 1]; }  // i even
 };
+
+// For the output pair at columns (c, c+1), c even, and tap distance d:
+// (v[c-d] + v[c+d], v[c+1-d] + v[c+1+d]).
+template <int NV>
+__device__ __forceinline__ float2 psum(const PairRow<NV>& V, int c, int d) {
+  if ((d & 1) == 0) return add2(V.pr(c - d), V.pr(c + d));
+  return make_float2(V.el(c - d) + V.el(c + d), V.el(c + 1 - d) + V.el(c + 1 + d));
+}
+
+// (fma(A[c+d], B[c+d], L[c-d]), fma(A[c+1+d], B[c+1+d], L[c+1-d])): the reference's
+// ((Xl*Yl) + (Xr*Yr)) form of the squared and cross moments with L = A*B precomputed.
+template <int NV>
+__device__ __forceinline__ float2 pfma(const PairRow<NV>& A, const PairRow<NV>& B,
+                                       const PairRow<NV>& L, int c, int d) {
+  if ((d & 1) == 0) return fma2(A.pr(c + d), B.pr(c + d), L.pr(c - d));
+  return make_float2(fmaf(A.el(c + d), B.el(c + d), L.el(c - d)),
+                     fmaf(A.el(c + 1 + d), B.el(c + 1 + d), L.el(c + 1 - d)));
+}
 
 // Store a pair of adjacent columns (gx, gx+1) of one row; `pair` means both columns are in
 // range and the address is aligned for a vector store.
@@ -479,56 +495,36 @@ __device__ __forceinline__ void fwd_hpass(const TIn* sx, const TIn* sy, float* r
           XY.a[q] = mul2(X.a[q], Y.a[q]);
           YY.a[q] = MERGED ? fma2(Y.a[q], Y.a[q], XX.a[q]) : mul2(Y.a[q], Y.a[q]);
         }
-#pragma unroll
-        for (int q = 0; q < NV / 2 - 1; ++q) {
-          XX.s[q] = mul2(X.s[q], X.s[q]);
-          XY.s[q] = mul2(X.s[q], Y.s[q]);
-          YY.s[q] = MERGED ? fma2(Y.s[q], Y.s[q], XX.s[q]) : mul2(Y.s[q], Y.s[q]);
-        }
         float* dst = ring + (hdst + i) * RP + 8 * j;
-        if constexpr (MERGED) {
-          // YY holds x^2 + y^2; ring maps: 0 = X, 1 = X^2+Y^2, 2 = Y, 3 = XY
-#pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            const int c = HA + 2 * p;
-            float2 sX = make_float2(0.f, 0.f), sS = sX, sY = sX, sXY = sX;
-#pragma unroll
-            for (int d = 1; d <= HALO; ++d) {
-              const float2 w = T.w[HALO - d];
-              const int l = c - d, r = c + d;
-              sX = fma2(add2(X.at(l), X.at(r)), w, sX);
-              sS = fma2(add2(YY.at(l), YY.at(r)), w, sS);
-              sY = fma2(add2(Y.at(l), Y.at(r)), w, sY);
-              sXY = fma2(fma2(X.at(r), Y.at(r), XY.at(l)), w, sXY);
-            }
-            const float2 wc = T.w[HALO];
-            *reinterpret_cast<float2*>(dst + 0 * kStrip + 2 * p) = fma2(X.at(c), wc, sX);
-            *reinterpret_cast<float2*>(dst + 1 * kStrip + 2 * p) = fma2(YY.at(c), wc, sS);
-            *reinterpret_cast<float2*>(dst + 2 * kStrip + 2 * p) = fma2(Y.at(c), wc, sY);
-            *reinterpret_cast<float2*>(dst + 3 * kStrip + 2 * p) = fma2(XY.at(c), wc, sXY);
-          }
-          continue;
-        }
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          const int c = HA + 2 * p;  // first column of the output pair
-          float2 sX = make_float2(0.f, 0.f), sX2 = sX, sY = sX, sY2 = sX, sXY = sX;
+          const int c = HA + 2 * p;  // first column of the output pair (even)
+          const float2 wc = T.w[HALO];
+          float2 sX = make_float2(0.f, 0.f), sY = sX, sXY = sX, s2a = sX, s2b = sX;
 #pragma unroll
           for (int d = 1; d <= HALO; ++d) {
             const float2 w = T.w[HALO - d];
-            const int l = c - d, r = c + d;
-            sX = fma2(add2(X.at(l), X.at(r)), w, sX);
-            sX2 = fma2(fma2(X.at(r), X.at(r), XX.at(l)), w, sX2);
-            sY = fma2(add2(Y.at(l), Y.at(r)), w, sY);
-            sY2 = fma2(fma2(Y.at(r), Y.at(r), YY.at(l)), w, sY2);
-            sXY = fma2(fma2(X.at(r), Y.at(r), XY.at(l)), w, sXY);
+            sX = fma2(psum(X, c, d), w, sX);
+            sY = fma2(psum(Y, c, d), w, sY);
+            sXY = fma2(pfma(X, Y, XY, c, d), w, sXY);
+            if constexpr (MERGED) {
+              s2a = fma2(psum(YY, c, d), w, s2a);  // YY holds x^2 + y^2
+            } else {
+              s2a = fma2(pfma(X, X, XX, c, d), w, s2a);
+              s2b = fma2(pfma(Y, Y, YY, c, d), w, s2b);
+            }
           }
-          const float2 wc = T.w[HALO];
-          *reinterpret_cast<float2*>(dst + 0 * kStrip + 2 * p) = fma2(X.at(c), wc, sX);
-          *reinterpret_cast<float2*>(dst + 1 * kStrip + 2 * p) = fma2(XX.at(c), wc, sX2);
-          *reinterpret_cast<float2*>(dst + 2 * kStrip + 2 * p) = fma2(Y.at(c), wc, sY);
-          *reinterpret_cast<float2*>(dst + 3 * kStrip + 2 * p) = fma2(YY.at(c), wc, sY2);
-          *reinterpret_cast<float2*>(dst + 4 * kStrip + 2 * p) = fma2(XY.at(c), wc, sXY);
+          // ring maps: MERGED 0 = X, 1 = X^2+Y^2, 2 = Y, 3 = XY; else X, X^2, Y, Y^2, XY
+          *reinterpret_cast<float2*>(dst + 0 * kStrip + 2 * p) = fma2(X.pr(c), wc, sX);
+          *reinterpret_cast<float2*>(dst + 2 * kStrip + 2 * p) = fma2(Y.pr(c), wc, sY);
+          if constexpr (MERGED) {
+            *reinterpret_cast<float2*>(dst + 1 * kStrip + 2 * p) = fma2(YY.pr(c), wc, s2a);
+            *reinterpret_cast<float2*>(dst + 3 * kStrip + 2 * p) = fma2(XY.pr(c), wc, sXY);
+          } else {
+            *reinterpret_cast<float2*>(dst + 1 * kStrip + 2 * p) = fma2(XX.pr(c), wc, s2a);
+            *reinterpret_cast<float2*>(dst + 3 * kStrip + 2 * p) = fma2(YY.pr(c), wc, s2b);
+            *reinterpret_cast<float2*>(dst + 4 * kStrip + 2 * p) = fma2(XY.pr(c), wc, sXY);
+          }
         }
       }
     }
@@ -750,9 +746,8 @@ __device__ __forceinline__ void bwd_hpass(const TP* sp, const float* sdl, float*
             const int c = HA + 2 * p;
             float2 s = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int d = 1; d <= HALO; ++d)
-              s = fma2(add2(V.at(c - d), V.at(c + d)), T.w[HALO - d], s);
-            *reinterpret_cast<float2*>(dst + m * kStrip + 2 * p) = fma2(V.at(c), T.w[HALO], s);
+            for (int d = 1; d <= HALO; ++d) s = fma2(psum(V, c, d), T.w[HALO - d], s);
+            *reinterpret_cast<float2*>(dst + m * kStrip + 2 * p) = fma2(V.pr(c), T.w[HALO], s);
           }
         }
       }
