@@ -43,6 +43,7 @@ namespace fssim {
 constexpr int kThreads = 128;         // 4 warps per CTA
 constexpr int kStrip = 64;            // output columns per strip
 constexpr int kRows = 32;             // output rows per step (8 per warp)
+constexpr int kRPT = kRows / 4;       // output rows per thread in the V-pass (4 warps)
 constexpr int kLeft = 8;              // staged columns left of the strip (>= HALO, 16-byte aligned)
 constexpr int kInCols = kStrip + 2 * kLeft;  // 80 staged columns
 constexpr double kFixScale = 268435456.0;    // 2^28 fixed point for the sums
@@ -111,6 +112,14 @@ __device__ __forceinline__ float2 sub2(float2 a, float2 b) {
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ float2 splat(float v) { return make_float2(v, v); }
+
+// Single-instruction reciprocal (PTX rcp.approx.ftz.f32, max error 1 ulp). The SSIM
+// denominators are >= C1 or C2 - O(1e-8), far above the denormal range.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
 
 // ---------------------------------------------------------------------------------------
 // Small device helpers
@@ -196,7 +205,8 @@ __device__ __forceinline__ float2 pfma(const PairRow<NV>& A, const PairRow<NV>& 
 
 // Store a pair of adjacent columns (gx, gx+1) of one row; `pair` means both columns are in
 // range and the address is aligned for a vector store.
-__device__ __forceinline__ void store2(float* base, int64_t idx, float2 v, bool pair, bool in0,
+template <typename I>
+__device__ __forceinline__ void store2(float* base, I idx, float2 v, bool pair, bool in0,
                                       bool in1) {
   if (pair) {
     *reinterpret_cast<float2*>(base + idx) = v;
@@ -205,7 +215,8 @@ __device__ __forceinline__ void store2(float* base, int64_t idx, float2 v, bool 
     if (in1) base[idx + 1] = v.y;
   }
 }
-__device__ __forceinline__ void store2(__half* base, int64_t idx, float2 v, bool pair, bool in0,
+template <typename I>
+__device__ __forceinline__ void store2(__half* base, I idx, float2 v, bool pair, bool in0,
                                       bool in1) {
   if (pair) {
     *reinterpret_cast<__half2*>(base + idx) = __floats2half2_rn(v.x, v.y);
@@ -214,7 +225,8 @@ __device__ __forceinline__ void store2(__half* base, int64_t idx, float2 v, bool
     if (in1) base[idx + 1] = __float2half_rn(v.y);
   }
 }
-__device__ __forceinline__ void store2(__nv_bfloat16* base, int64_t idx, float2 v, bool pair,
+template <typename I>
+__device__ __forceinline__ void store2(__nv_bfloat16* base, I idx, float2 v, bool pair,
                                       bool in0, bool in1) {
   if (pair) {
     *reinterpret_cast<__nv_bfloat162*>(base + idx) = __floats2bfloat162_rn(v.x, v.y);
@@ -224,8 +236,8 @@ __device__ __forceinline__ void store2(__nv_bfloat16* base, int64_t idx, float2 
   }
 }
 
-template <typename T>
-__device__ __forceinline__ float2 load2(const T* base, int64_t idx, bool pair, bool in0, bool in1) {
+template <typename T, typename I>
+__device__ __forceinline__ float2 load2(const T* base, I idx, bool pair, bool in0, bool in1) {
   if (pair) {
     if constexpr (sizeof(T) == 4) {
       return __ldg(reinterpret_cast<const float2*>(base + idx));
@@ -415,16 +427,21 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
 // Vertical 2*HALO+1 tap sum of column pairs for 8 consecutive output rows: rows k..k+2HALO
 // of `v` feed output k (reference order: pairs d = 1..HALO, centre last).
 template <int HALO, bool HW_>
-__device__ __forceinline__ void vsum8(const float2 (&v)[8 + 2 * HALO], float2 (&o)[8],
+__device__ __forceinline__ void vsumR(const float2 (&v)[kRPT + 2 * HALO], float2 (&o)[kRPT],
                                       const Taps2<HALO, HW_>& T) {
+  // Tap distance outermost: the kRPT independent accumulation chains advance together, so
+  // consecutive packed FMAs never wait on each other.
+  float2 acc[kRPT];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    float2 acc = make_float2(0.f, 0.f);
+  for (int k = 0; k < kRPT; ++k) acc[k] = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int d = 1; d <= HALO; ++d)
-      acc = fma2(add2(v[k + HALO - d], v[k + HALO + d]), T.w[HALO - d], acc);
-    o[k] = fma2(v[k + HALO], T.w[HALO], acc);
+  for (int d = 1; d <= HALO; ++d) {
+#pragma unroll
+    for (int k = 0; k < kRPT; ++k)
+      acc[k] = fma2(add2(v[k + HALO - d], v[k + HALO + d]), T.w[HALO - d], acc[k]);
   }
+#pragma unroll
+  for (int k = 0; k < kRPT; ++k) o[k] = fma2(v[k + HALO], T.w[HALO], acc[k]);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -551,7 +568,7 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   const int64_t end = (g.LT * (blockIdx.x + 1)) / gridDim.x;
   const TIn* const src[2] = {static_cast<const TIn*>(a.img1), static_cast<const TIn*>(a.img2)};
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int r0 = warp * 8;
+  const int r0 = warp * kRPT;
   const float2 C1v = splat(a.C1), C2v = splat(a.C2), two = splat(2.f);
   Taps2<HALO, HW_> T;
   T.load();
@@ -570,14 +587,14 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
 
     // ---- V-pass + epilogue: rows r0..r0+7 of the step, columns 2*lane, 2*lane+1 ----
     if (r0 < cur.n) {
-      float2 res[NM][8];
+      float2 res[NM][kRPT];
 #pragma unroll
       for (int m = 0; m < NM; ++m) {
-        float2 v[8 + 2 * HALO];
+        float2 v[kRPT + 2 * HALO];
 #pragma unroll
-        for (int q = 0; q < 8 + 2 * HALO; ++q)
+        for (int q = 0; q < kRPT + 2 * HALO; ++q)
           v[q] = *reinterpret_cast<const float2*>(ring + (r0 + q) * RP + m * kStrip + 2 * lane);
-        vsum8<HALO, HW_>(v, res[m], T);
+        vsumR<HALO, HW_>(v, res[m], T);
       }
       const int gx0 = cur.strip * kStrip + 2 * lane;
       const int W = static_cast<int>(g.W);
@@ -586,32 +603,46 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
       // columns counted in the reduction / receiving gradient (valid crop)
       const bool col0 = in0 && (!a.valid || (gx0 >= HALO && gx0 < W - HALO));
       const bool col1 = in1 && (!a.valid || (gx0 + 1 >= HALO && gx0 + 1 < W - HALO));
+      // step rows inside the valid crop: [rlo, rhi) in step-local row numbers
+      int rlo = 0, rhi = cur.n;
+      if (a.valid) {
+        rlo = max(0, HALO - cur.t);
+        rhi = min(cur.n, static_cast<int>(g.H) - HALO - cur.t);
+      }
+      // outputs addressed as plane base + 32-bit in-plane offset (planes < 2^31 elements)
       const int64_t plane_off = cur.plane * g.HW;
+      const int off0 = (cur.t + r0) * W + gx0;
+      float* mapp = a.map ? a.map + plane_off : nullptr;
+      TP* q0 = TRAIN ? static_cast<TP*>(a.p0) + plane_off : nullptr;
+      TP* q1 = TRAIN ? static_cast<TP*>(a.p1) + plane_off : nullptr;
+      TP* q2 = TRAIN ? static_cast<TP*>(a.p2) + plane_off : nullptr;
+      const float2 neg1 = splat(-1.f);
       float step_sum = 0.f;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < kRPT; ++k) {
         const int row = r0 + k;
         if (row < cur.n) {
-          const int gy = cur.t + row;
-          const bool row_ok = !a.valid || (gy >= HALO && gy < g.H - HALO);
+          const bool row_ok = row >= rlo && row < rhi;
           const float2 mu1 = res[0][k], mu2 = res[2][k];
           const float2 mu1_sq = mul2(mu1, mu1), mu2_sq = mul2(mu2, mu2);
           const float2 msq = add2(mu1_sq, mu2_sq);
+          const float2 mu12 = mul2(mu1, mu2);
           const float2 A = add2(msq, C1v);
           float2 B, sigma12;
+          // differences as fma(b, -1, a): the same single rounding as a - b
           if constexpr (MERGED) {
-            B = add2(sub2(res[1][k], msq), C2v);
-            sigma12 = sub2(res[3][k], mul2(mu1, mu2));
+            B = add2(fma2(msq, neg1, res[1][k]), C2v);
+            sigma12 = fma2(mu12, neg1, res[3][k]);
           } else {
-            const float2 sigma1_sq = sub2(res[1][k], mu1_sq);
-            const float2 sigma2_sq = sub2(res[3][k], mu2_sq);
+            const float2 sigma1_sq = fma2(mu1_sq, neg1, res[1][k]);
+            const float2 sigma2_sq = fma2(mu2_sq, neg1, res[3][k]);
             B = add2(add2(sigma1_sq, sigma2_sq), C2v);
-            sigma12 = sub2(res[NM - 1][k], mul2(mu1, mu2));
+            sigma12 = fma2(mu12, neg1, res[NM - 1][k]);
           }
-          const float2 Cc = fma2(mul2(two, mu1), mu2, C1v);
+          const float2 Cc = fma2(two, mu12, C1v);
           const float2 D = fma2(two, sigma12, C2v);
-          const float2 rA = make_float2(__fdividef(1.f, A.x), __fdividef(1.f, A.y));
-          const float2 rB = make_float2(__fdividef(1.f, B.x), __fdividef(1.f, B.y));
+          const float2 rA = make_float2(rcp_approx(A.x), rcp_approx(A.y));
+          const float2 rB = make_float2(rcp_approx(B.x), rcp_approx(B.y));
           const float2 rAB = mul2(rA, rB);
           const float2 v = mul2(mul2(Cc, D), rAB);
           const bool c0 = row_ok && col0, c1 = row_ok && col1;
@@ -620,20 +651,22 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
             const float v1 = (a.clamp && v.y < 0.f) ? 0.f : v.y;
             step_sum += (c0 ? v0 : 0.f) + (c1 ? v1 : 0.f);
           }
-          const int64_t idx = plane_off + static_cast<int64_t>(gy) * g.W + gx0;
-          if (a.map) store2(a.map, idx, v, pair, in0, in1);
+          const int off = off0 + k * W;
+          if (mapp) store2(mapp, off, v, pair, in0, in1);
           if (TRAIN) {
             const bool live0 = !a.mask_partials || (c0 && (!a.clamp || v.x >= 0.f));
             const bool live1 = !a.mask_partials || (c1 && (!a.clamp || v.y >= 0.f));
-            float2 pm = fma2(mul2(two, mu2), mul2(sub2(D, Cc), rAB),
-                             mul2(mul2(two, mu1), mul2(v, sub2(rB, rA))));
-            float2 ps = mul2(make_float2(-v.x, -v.y), rB);
+            // dm/dmu1 = 2 mu2 (D - C) / (AB) + 2 mu1 v (1/B - 1/A); dm/dsigma1^2 = -v / B;
+            // dm/dsigma12 = 2 C / (AB)   (csrc/ssim.cu:323-330, with v = CD/(AB))
+            float2 pm = fma2(mul2(two, mu2), mul2(fma2(Cc, neg1, D), rAB),
+                             mul2(mul2(two, mu1), mul2(v, fma2(rA, neg1, rB))));
+            float2 ps = mul2(mul2(v, neg1), rB);
             float2 pc = mul2(mul2(two, Cc), rAB);
             if (!live0) pm.x = ps.x = pc.x = 0.f;
             if (!live1) pm.y = ps.y = pc.y = 0.f;
-            store2(static_cast<TP*>(a.p0), idx, pm, pair, in0, in1);
-            store2(static_cast<TP*>(a.p1), idx, ps, pair, in0, in1);
-            store2(static_cast<TP*>(a.p2), idx, pc, pair, in0, in1);
+            store2(q0, off, pm, pair, in0, in1);
+            store2(q1, off, ps, pair, in0, in1);
+            store2(q2, off, pc, pair, in0, in1);
           }
         }
       }
@@ -741,14 +774,19 @@ __device__ __forceinline__ void bwd_hpass(const TP* sp, const float* sdl, float*
           }
           PairRow<NV> V;
           V.build(v);
+          float2 s4[4];
 #pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            const int c = HA + 2 * p;
-            float2 s = make_float2(0.f, 0.f);
+          for (int p = 0; p < 4; ++p) s4[p] = make_float2(0.f, 0.f);
+          // tap distance outermost: the 4 output pairs' chains advance together
 #pragma unroll
-            for (int d = 1; d <= HALO; ++d) s = fma2(psum(V, c, d), T.w[HALO - d], s);
-            *reinterpret_cast<float2*>(dst + m * kStrip + 2 * p) = fma2(V.pr(c), T.w[HALO], s);
+          for (int d = 1; d <= HALO; ++d) {
+#pragma unroll
+            for (int p = 0; p < 4; ++p) s4[p] = fma2(psum(V, HA + 2 * p, d), T.w[HALO - d], s4[p]);
           }
+#pragma unroll
+          for (int p = 0; p < 4; ++p)
+            *reinterpret_cast<float2*>(dst + m * kStrip + 2 * p) =
+                fma2(V.pr(HA + 2 * p), T.w[HALO], s4[p]);
         }
       }
     }
@@ -776,7 +814,7 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
   const TIn* img1 = static_cast<const TIn*>(a.img1);
   const TIn* img2 = static_cast<const TIn*>(a.img2);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int r0 = warp * 8;
+  const int r0 = warp * kRPT;
   const float2 two = splat(2.f);
   Taps2<HALO, HW_> T;
   T.load();
@@ -805,44 +843,46 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
       const int64_t plane_off = cur.plane * g.HW;
       // Issue the epilogue's image loads before the vertical pass so they are in flight
       // while it runs.
-      const int64_t row_base = plane_off + static_cast<int64_t>(cur.t + r0) * g.W + gx0;
-      float2 xin[8], yin[8];
+      // plane base + 32-bit in-plane offsets (planes < 2^31 elements)
+      const int off0 = (cur.t + r0) * W + gx0;
+      const TIn* x_pl = img1 + plane_off;
+      const TIn* y_pl = img2 + plane_off;
+      float2 xin[kRPT], yin[kRPT];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < kRPT; ++k) {
         xin[k] = make_float2(0.f, 0.f);
         yin[k] = xin[k];
         if (r0 + k < cur.n) {
-          const int64_t idx = row_base + k * g.W;
-          xin[k] = load2(img1, idx, pair, in0, in1);
-          yin[k] = load2(img2, idx, pair, in0, in1);
+          xin[k] = load2(x_pl, off0 + k * W, pair, in0, in1);
+          yin[k] = load2(y_pl, off0 + k * W, pair, in0, in1);
         }
       }
       float2 chain = splat(a.chain_scale);
       if (!DLMAP && a.grad_out) {
         chain = mul2(chain, splat(a.grad_out[a.grad_per_image ? cur.img : 0]));
       }
-      float2 res[3][8];
+      float2 res[3][kRPT];
 #pragma unroll
       for (int m = 0; m < 3; ++m) {
-        float2 v[8 + 2 * HALO];
+        float2 v[kRPT + 2 * HALO];
 #pragma unroll
-        for (int q = 0; q < 8 + 2 * HALO; ++q)
+        for (int q = 0; q < kRPT + 2 * HALO; ++q)
           v[q] = *reinterpret_cast<const float2*>(ring + (r0 + q) * RP + m * kStrip + 2 * lane);
-        vsum8<HALO, HW_>(v, res[m], T);
+        vsumR<HALO, HW_>(v, res[m], T);
       }
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < kRPT; ++k) {
         const int row = r0 + k;
         if (row < cur.n) {
-          const int64_t idx = row_base + k * g.W;
+          const int off = off0 + k * W;
           float2 gv = fma2(yin[k], res[2][k], fma2(mul2(two, xin[k]), res[1][k], res[0][k]));
           if (!DLMAP) gv = mul2(gv, chain);
           if (a.grad_dtype == 0)
-            store2(static_cast<float*>(a.grad), idx, gv, pair, in0, in1);
+            store2(static_cast<float*>(a.grad) + plane_off, off, gv, pair, in0, in1);
           else if (a.grad_dtype == 1)
-            store2(static_cast<__half*>(a.grad), idx, gv, pair, in0, in1);
+            store2(static_cast<__half*>(a.grad) + plane_off, off, gv, pair, in0, in1);
           else
-            store2(static_cast<__nv_bfloat16*>(a.grad), idx, gv, pair, in0, in1);
+            store2(static_cast<__nv_bfloat16*>(a.grad) + plane_off, off, gv, pair, in0, in1);
         }
       }
     }
