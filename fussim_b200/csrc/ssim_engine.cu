@@ -2,6 +2,7 @@
 // window size / element types, and the extern "C" entry points declared in
 // include/fussim_b200.h. No torch, no Python: any host language can bind this library.
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <climits>
 #include <cstdint>
@@ -110,6 +111,63 @@ int grid_size(const fssim::Geometry& g, int occ, int sms) {
   return static_cast<int>(grid);
 }
 
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime (the library
+// does not link libcuda). nullptr if the driver does not provide it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    (void)cudaGetLastError();
+  });
+  return fn;
+}
+
+// Tensor map for the kernels' TMA staging: the batch as a (planes, H, W) tensor of
+// FP32 or FP16 elements, boxes of kBoxRows rows x one staged row pitch of columns,
+// zero fill outside. False (the kernels then stage with cp.async) when the layout does not
+// meet the copy unit's rules: 16-byte aligned base, row pitch a multiple of 16 bytes.
+bool encode_rows(CUtensorMap* m, const void* base, size_t esize, const fssim::Geometry& g) {
+  const PFN_cuTensorMapEncodeTiled_v12000 fn = tensor_map_encoder();
+  if (!fn || !base || !aligned(base, 16)) return false;
+  if ((static_cast<size_t>(g.W) * esize) % 16 != 0) return false;
+  const int64_t planes = static_cast<int64_t>(g.B) * g.C;
+  if (planes < 1 || planes > INT_MAX || g.H < 1 || g.W < 1) return false;
+  const bool f32 = esize == 4;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(g.W), static_cast<cuuint64_t>(g.H),
+                        static_cast<cuuint64_t>(planes)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(g.W) * esize,
+                           static_cast<cuuint64_t>(g.HW) * esize};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(f32 ? fssim::StagePitch<float>::value
+                                                   : fssim::StagePitch<__half>::value),
+                       static_cast<cuuint32_t>(fssim::kBoxRows), 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r =
+      fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Sets p.use_tma when every staged tensor of the forward has a tensor map.
+void set_fwd_tma(fssim::FwdParams& p, size_t esize) {
+  p.use_tma = encode_rows(&p.tmap[0], p.img1, esize, p.g) &&
+              encode_rows(&p.tmap[1], p.img2, esize, p.g);
+}
+void set_bwd_tma(fssim::BwdParams& p, size_t pesize) {
+  bool ok = encode_rows(&p.tmap[0], p.p0, pesize, p.g) &&
+            encode_rows(&p.tmap[1], p.p1, pesize, p.g) &&
+            encode_rows(&p.tmap[2], p.p2, pesize, p.g);
+  if (ok && p.dl) ok = encode_rows(&p.tmap[3], p.dl, sizeof(float), p.g);
+  p.use_tma = ok;
+}
+
 int launch_error(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
@@ -209,6 +267,7 @@ int compat_forward(int ws, float C1, float C2, const TIn* img1, const TIn* img2,
   p.aligned16 = (W % E == 0) && aligned(img1, 16) && aligned(img2, 16);
   p.pair_ok = (W % 2 == 0) && aligned(map, 8) &&
               (!train || (aligned(p0, 8) && aligned(p1, 8) && aligned(p2, 8)));
+  set_fwd_tma(p, sizeof(TIn));
   if (train) return dispatch_fwd<TIn, float, true, false>(ws, p, stream);
   return dispatch_fwd<TIn, float, false, false>(ws, p, stream);
 }
@@ -242,6 +301,7 @@ int compat_backward(int ws, const TIn* img1, const TIn* img2, const float* dl, c
                 aligned(p2, 16);
   p.pair_ok = (W % 2 == 0) && aligned(img1, 2 * sizeof(TIn)) && aligned(img2, 2 * sizeof(TIn)) &&
               aligned(grad, 8);
+  set_bwd_tma(p, sizeof(float));
   return dispatch_bwd<TIn, float, true>(ws, p, stream);
 }
 
@@ -266,6 +326,23 @@ const char* fssim_status_string(int status) {
 const char* fssim_last_error(void) { return g_last_error.c_str(); }
 
 const char* fssim_version(void) { return "0.1.0"; }
+
+int fssim_poll_device_error(unsigned* code, int clear) {
+  g_last_error.clear();
+  if (!code) return fail(FSSIM_ERR_NULLPTR, "code is NULL");
+  unsigned v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, fssim::g_device_error, sizeof(v));
+  if (e != cudaSuccess)
+    return fail(FSSIM_ERR_CUDA, std::string("reading the device error flag: ") + cudaGetErrorString(e));
+  if (clear && v) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(fssim::g_device_error, &zero, sizeof(zero));
+    if (e != cudaSuccess)
+      return fail(FSSIM_ERR_CUDA, std::string("clearing the device error flag: ") + cudaGetErrorString(e));
+  }
+  *code = v;
+  return FSSIM_OK;
+}
 
 int fssim_fusedssim(int window_size, float C1, float C2, const float* img1, const float* img2,
                     int64_t B, int64_t C, int64_t H, int64_t W, int train, float* ssim_map,
@@ -393,6 +470,7 @@ int fssim_forward(const fssim_forward_args* a, fssim_stream_t stream) {
   bool pair = (a->W % 2 == 0) && (!a->ssim_map || aligned(a->ssim_map, 8));
   if (a->train) pair = pair && aligned(p.p0, 2 * PE) && aligned(p.p1, 2 * PE) && aligned(p.p2, 2 * PE);
   p.pair_ok = pair;
+  set_fwd_tma(p, E);
 
   const int ws = a->window_size;
   cudaStream_t s = stream;
@@ -443,6 +521,7 @@ int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
                 aligned(p.p1, 16) && aligned(p.p2, 16);
   p.pair_ok = (a->W % 2 == 0) && aligned(a->img1, 2 * E) && aligned(a->img2, 2 * E) &&
               aligned(a->grad, 2 * GE);
+  set_bwd_tma(p, PE);
   const int ws = a->window_size;
   cudaStream_t s = stream;
   if (a->dtype == FSSIM_F32) return dispatch_bwd<float, float, false>(ws, p, s);

@@ -6,13 +6,13 @@
 // strips of 64 output columns. Every (plane, strip) pair is a column of H output rows;
 // all columns laid end to end form LT = P*S*H "strip-rows". A persistent grid of G CTAs
 // splits [0, LT) into G equal contiguous ranges, so every CTA gets the same number of
-// rows whatever the image shape. A CTA walks its range in steps of up to 32 output rows:
+// rows whatever the image shape. A CTA walks its range in steps of up to 16 output rows:
 //
 //   stage   input rows of the step (64 + 16 columns, zero outside the image) -> smem,
 //           issued with cp.async one step ahead so the copy overlaps the previous step;
 //   H-pass  horizontal Gaussian of every staged row -> a smem ring of moment rows
 //           (5 moments forward, 3 partials backward);
-//   V-pass  vertical Gaussian of the ring for the step's 32 x 64 outputs, then the
+//   V-pass  vertical Gaussian of the ring for the step's 16 x 64 outputs, then the
 //           per-pixel epilogue (SSIM + partials, or the gradient).
 //
 // The last 2*HALO moment rows of a step are kept for the next step (copied to the top
@@ -33,6 +33,7 @@
 // (atomicInc ticket) turns the accumulators into the outputs and zeroes them again.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (type only; the driver API is not linked)
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -42,7 +43,7 @@ namespace fssim {
 
 constexpr int kThreads = 128;         // 4 warps per CTA
 constexpr int kStrip = 64;            // output columns per strip
-constexpr int kRows = 32;             // output rows per step (8 per warp)
+constexpr int kRows = 16;             // output rows per step
 constexpr int kRPT = kRows / 4;       // output rows per thread in the V-pass (4 warps)
 constexpr int kLeft = 8;              // staged columns left of the strip (>= HALO, 16-byte aligned)
 constexpr int kInCols = kStrip + 2 * kLeft;  // 80 staged columns
@@ -55,11 +56,17 @@ template <> struct StagePitch<float> { static constexpr int value = 84; };   // 
 template <> struct StagePitch<__half> { static constexpr int value = 88; };  // 44 words
 
 // Moment-ring pitch in floats: NMAP rows of 64 plus 2. The H-pass stores 8-byte column
-// pairs from 32 consecutive rows per warp instruction; a pitch of 2 mod 32 words puts each
-// half warp on 32 distinct banks.
+// pairs from 16 consecutive rows per half warp; a pitch of 2 mod 32 words puts each half
+// warp on 32 distinct banks.
 template <int NMAP> struct RingPitch { static constexpr int value = NMAP * kStrip + 2; };
 
 template <int HALO> struct MaxRows { static constexpr int value = kRows + 2 * HALO; };
+
+// Staged rows per map: MaxRows rounded up to whole TMA boxes of 8 rows. The map stride
+// (rows x pitch x element size) is then a multiple of 128 bytes, as is every box start.
+template <int HALO> struct StageRows {
+  static constexpr int value = (MaxRows<HALO>::value + 7) / 8 * 8;
+};
 
 // Gaussian taps: [half-rounded][halo-3][k], k = 0..2*HALO, symmetric.
 // Row 0: the reference's FP32 tables (csrc/ssim.cu:28-64).
@@ -138,6 +145,64 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, bool in) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// Staging with the tensor memory accelerator (TMA)
+// ---------------------------------------------------------------------------------------
+// When every staged plane is 16-byte aligned with a row pitch that is a multiple of 16
+// bytes, one thread stages a step with a handful of tiled bulk copies (boxes of kBoxRows
+// rows x one staged row pitch of columns, zero-filled outside the image by the copy unit)
+// that complete on an mbarrier. This replaces 2-4 cp.async chunks per thread per staged
+// row and all their address arithmetic. The copies never use cluster multicast.
+constexpr int kBoxRows = 8;
+constexpr int kWaitLimit = 1 << 20;  // bounded mbarrier polls before a step reports failure
+
+// Device-side failure codes (OR-ed into g_device_error, read by fssim_poll_device_error).
+constexpr unsigned kErrStagingTimeout = 1u;
+__device__ unsigned g_device_error;
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+// Orders this CTA's earlier generic-proxy shared-memory accesses before later bulk copies.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for the mbarrier phase with the given parity to complete; false after kWaitLimit
+// polls (the caller reports the failure and leaves the kernel).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
+  for (int i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+// One 3-D tiled bulk copy global -> shared (coordinates: column, row, plane).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y,
+                                            int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ float to_f(float v) { return v; }
@@ -268,7 +333,7 @@ struct Step {
   int chan;       // channel of the plane (plane % C)
   int strip;
   int t;          // first output row of this step
-  int n;          // output rows in this step (1..32); 0 = no step
+  int n;          // output rows in this step (1..kRows); 0 = no step
   int h0;         // first moment row computed by this step
   int nh;         // moment rows computed by this step
   int hdst;       // ring row receiving moment row h0
@@ -402,10 +467,35 @@ __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const 
   cp_async_commit();
 }
 
-// Copy ring rows [32, 32 + 2*HALO) to [0, 2*HALO): the vertical halo for the next step.
-// Only full 32-row steps carry, so source and destination are disjoint contiguous blocks.
+// Bytes the TMA staging of one step delivers for NMAP maps of element type T.
+template <typename T, int NMAP>
+__device__ __forceinline__ unsigned tma_step_bytes(int nh) {
+  const int nbox = (nh + kBoxRows - 1) / kBoxRows;
+  return static_cast<unsigned>(NMAP * nbox * kBoxRows * StagePitch<T>::value * sizeof(T));
+}
+
+// TMA staging of one step, issued by a single thread: rows [h0, h0+nh) rounded up to whole
+// boxes, columns [x0-8, x0-8+pitch) of plane s.plane for each of the NMAP tensor maps, into
+// the layout [NMAP][SROWS][pitch]. Rows or columns outside the image arrive as zeros.
+template <typename T, int NMAP, int SROWS>
+__device__ __forceinline__ void stage_tma(T* sm, const CUtensorMap* maps, const Step& s,
+                                          uint64_t* bar) {
+  constexpr int P = StagePitch<T>::value;
+  const int nbox = (s.nh + kBoxRows - 1) / kBoxRows;
+  const int x0 = s.strip * kStrip - kLeft;
+  const int z = static_cast<int>(s.plane);
+#pragma unroll
+  for (int m = 0; m < NMAP; ++m)
+    for (int b = 0; b < nbox; ++b)
+      tma_load_3d(sm + (m * SROWS + b * kBoxRows) * P, maps + m, x0, s.h0 + b * kBoxRows, z, bar);
+}
+
+// Copy ring rows [kRows, kRows + 2*HALO) to [0, 2*HALO): the vertical halo for the next
+// step. Only full steps carry, and 2*HALO <= kRows, so source and destination are disjoint
+// contiguous blocks.
 template <int HALO, int RP>
 __device__ __forceinline__ void ring_carry(float* ring) {
+  static_assert(2 * HALO <= kRows, "carry source and destination must not overlap");
   static_assert((2 * HALO * RP) % 4 == 0 && (kRows * RP) % 4 == 0, "float4 carry");
   constexpr int N4 = 2 * HALO * RP / 4;
   const float4* src = reinterpret_cast<const float4*>(ring + kRows * RP);
@@ -448,6 +538,7 @@ __device__ __forceinline__ void vsumR(const float2 (&v)[kRPT + 2 * HALO], float2
 // Forward kernel
 // ---------------------------------------------------------------------------------------
 struct FwdParams {
+  CUtensorMap tmap[2];   // img1, img2 as (W, H, planes), boxes of 8 rows (when use_tma)
   const void* img1;
   const void* img2;
   float* map;            // optional per-pixel SSIM (unmasked)
@@ -460,7 +551,7 @@ struct FwdParams {
   unsigned* ticket;         // last-CTA ticket (workspace)
   Geometry g;
   float C1, C2, out_scale;
-  int valid, clamp, reduce, mask_partials, aligned16, pair_ok;
+  int valid, clamp, reduce, mask_partials, aligned16, pair_ok, use_tma;
 };
 
 // MERGED (the fused loss path): the SSIM value and its partials depend on the second moments
@@ -474,13 +565,16 @@ struct FwdConfig {
   static constexpr bool kHalfW = sizeof(TIn) == 2;
   static constexpr int kMaps = MERGED ? 4 : 5;
   static constexpr int kMaxR = MaxRows<HALO>::value;
+  static constexpr int kSRows = StageRows<HALO>::value;
   static constexpr int kSP = StagePitch<TIn>::value;
   static constexpr int kRP = RingPitch<kMaps>::value;
-  static constexpr size_t kStageBytes = 2ull * kMaxR * kSP * sizeof(TIn);
+  static constexpr size_t kStageBytes = 2ull * kSRows * kSP * sizeof(TIn);
   static constexpr size_t kRingBytes = static_cast<size_t>(kMaxR) * kRP * sizeof(float);
-  static constexpr size_t kSmem = kStageBytes + kRingBytes;
+  // + 128: the dynamic shared memory base is rounded up to 128 bytes for the TMA boxes
+  static constexpr size_t kSmem = kStageBytes + kRingBytes + 128;
   // resident CTAs per SM the kernel is compiled for (228 KB of shared memory per SM)
-  static constexpr int kMinBlocks = (kSmem + 1024) * 3 <= 228 * 1024 ? 3 : 2;
+  static constexpr int kFit = static_cast<int>((228 * 1024) / (kSmem + 1024));
+  static constexpr int kMinBlocks = kFit >= 4 ? 4 : (kFit >= 3 ? 3 : 2);
 };
 
 // Horizontal pass of the forward: for staged row i and output columns 8j..8j+7 compute the
@@ -494,12 +588,14 @@ __device__ __forceinline__ void fwd_hpass(const TIn* sx, const TIn* sy, float* r
   constexpr int HA = (sizeof(TIn) == 2 || HALO > 4) ? 8 : 4;  // aligned left extent
   constexpr int NV = 8 + 2 * HA;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int rg = 0; rg < nh; rg += 32) {
-    const int i = rg + lane;
+  // one task (row i, columns 8j..8j+7) per thread per group of kRows rows: lanes 0-15 and
+  // 16-31 of a warp take the same 16 rows in two column chunks
+  static_assert(kRows == 16, "task mapping assumes 16-row steps");
+  for (int rg = 0; rg < nh; rg += kRows) {
+    const int i = rg + (lane & (kRows - 1));
     if (i < nh) {
-#pragma unroll 1
-      for (int jj = 0; jj < 2; ++jj) {
-        const int j = warp + 4 * jj;
+      {
+        const int j = warp + 4 * (lane >> 4);
         float xv[NV], yv[NV];
         load_vec(sx + i * SP + 8 * j + kLeft - HA, xv);
         load_vec(sy + i * SP + 8 * j + kLeft - HA, yv);
@@ -550,18 +646,20 @@ __device__ __forceinline__ void fwd_hpass(const TIn* sx, const TIn* sy, float* r
 
 template <int HALO, typename TIn, typename TP, bool TRAIN, bool MERGED>
 __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MERGED>::kMinBlocks))
-    ssim_fwd_kernel(const FwdParams a) {
+    ssim_fwd_kernel(const __grid_constant__ FwdParams a) {
   using Cfg = FwdConfig<HALO, TIn, TP, TRAIN, MERGED>;
   constexpr int NM = Cfg::kMaps;
-  constexpr int MAXR = Cfg::kMaxR;
+  constexpr int SROWS = Cfg::kSRows;
   constexpr int SP = Cfg::kSP;
   constexpr int RP = Cfg::kRP;
   constexpr bool HW_ = Cfg::kHalfW;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  TIn* stg = reinterpret_cast<TIn*>(smem_raw);
-  float* ring = reinterpret_cast<float*>(smem_raw + Cfg::kStageBytes);
+  unsigned char* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
+  TIn* stg = reinterpret_cast<TIn*>(smem);
+  float* ring = reinterpret_cast<float*>(smem + Cfg::kStageBytes);
   __shared__ double red[4];
   __shared__ unsigned s_last;
+  __shared__ uint64_t bar;
 
   const Geometry& g = a.g;
   const int64_t beg = (g.LT * blockIdx.x) / gridDim.x;
@@ -573,17 +671,51 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   Taps2<HALO, HW_> T;
   T.load();
 
+  const bool tma = a.use_tma != 0;
+  if (tma && threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
   Step cur = first_step<HALO>(beg, end, g);
-  if (cur.n) stage<TIn, 2, MAXR>(stg, src, g, cur, a.aligned16);
+  if (cur.n) {
+    if (!tma) {
+      stage<TIn, 2, SROWS>(stg, src, g, cur, a.aligned16);
+    } else if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(cur.nh));
+      stage_tma<TIn, 2, SROWS>(stg, a.tmap, cur, &bar);
+    }
+  }
+  unsigned phase = 0;
   double run_sum = 0.0;
 
   while (cur.n) {
-    cp_async_wait_all();
-    __syncthreads();
-    fwd_hpass<HALO, TIn, MAXR, MERGED>(stg, stg + MAXR * SP, ring, cur.nh, cur.hdst, T);
+    bool timed_out = false;
+    if (tma) {
+      timed_out = !mbar_wait_bounded(&bar, phase);
+      phase ^= 1u;
+    } else {
+      cp_async_wait_all();
+    }
+    if (__syncthreads_or(timed_out)) {
+      // staging did not complete: report it, give the copies in flight one more bounded
+      // wait so none lands after the CTA has exited, and leave
+      if (threadIdx.x == 0) atomicOr(&g_device_error, kErrStagingTimeout);
+      mbar_wait_bounded(&bar, phase ^ 1u);
+      return;
+    }
+    fwd_hpass<HALO, TIn, SROWS, MERGED>(stg, stg + SROWS * SP, ring, cur.nh, cur.hdst, T);
     __syncthreads();
     const Step nxt = next_step<HALO>(cur, g);
-    if (nxt.n) stage<TIn, 2, MAXR>(stg, src, g, nxt, a.aligned16);
+    if (nxt.n) {
+      if (!tma) {
+        stage<TIn, 2, SROWS>(stg, src, g, nxt, a.aligned16);
+      } else if (threadIdx.x == 0) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(nxt.nh));
+        stage_tma<TIn, 2, SROWS>(stg, a.tmap, nxt, &bar);
+      }
+    }
 
     // ---- V-pass + epilogue: rows r0..r0+7 of the step, columns 2*lane, 2*lane+1 ----
     if (r0 < cur.n) {
@@ -617,56 +749,86 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
       TP* q1 = TRAIN ? static_cast<TP*>(a.p1) + plane_off : nullptr;
       TP* q2 = TRAIN ? static_cast<TP*>(a.p2) + plane_off : nullptr;
       const float2 neg1 = splat(-1.f);
+      // SSIM value and (TRAIN) its three partials for output row k of this thread
+      auto pixel = [&](int k, float2& v, float2& pm, float2& ps, float2& pc) {
+        const float2 mu1 = res[0][k], mu2 = res[2][k];
+        const float2 mu1_sq = mul2(mu1, mu1), mu2_sq = mul2(mu2, mu2);
+        const float2 msq = add2(mu1_sq, mu2_sq);
+        const float2 mu12 = mul2(mu1, mu2);
+        const float2 A = add2(msq, C1v);
+        float2 B, sigma12;
+        // differences as fma(b, -1, a): the same single rounding as a - b
+        if constexpr (MERGED) {
+          B = add2(fma2(msq, neg1, res[1][k]), C2v);
+          sigma12 = fma2(mu12, neg1, res[3][k]);
+        } else {
+          const float2 sigma1_sq = fma2(mu1_sq, neg1, res[1][k]);
+          const float2 sigma2_sq = fma2(mu2_sq, neg1, res[3][k]);
+          B = add2(add2(sigma1_sq, sigma2_sq), C2v);
+          sigma12 = fma2(mu12, neg1, res[NM - 1][k]);
+        }
+        const float2 Cc = fma2(two, mu12, C1v);
+        const float2 D = fma2(two, sigma12, C2v);
+        const float2 rA = make_float2(rcp_approx(A.x), rcp_approx(A.y));
+        const float2 rB = make_float2(rcp_approx(B.x), rcp_approx(B.y));
+        const float2 rAB = mul2(rA, rB);
+        v = mul2(mul2(Cc, D), rAB);
+        if (TRAIN) {
+          // dm/dmu1 = 2 mu2 (D - C) / (AB) + 2 mu1 v (1/B - 1/A); dm/dsigma1^2 = -v / B;
+          // dm/dsigma12 = 2 C / (AB)   (csrc/ssim.cu:323-330, with v = CD/(AB))
+          pm = fma2(mul2(two, mu2), mul2(fma2(Cc, neg1, D), rAB),
+                    mul2(mul2(two, mu1), mul2(v, fma2(rA, neg1, rB))));
+          ps = mul2(mul2(v, neg1), rB);
+          pc = mul2(mul2(two, Cc), rAB);
+        }
+      };
+      // A full step of a strip that lies inside the image (and inside the valid crop),
+      // without the clamp, needs no masks: every output is stored and summed as a pair.
+      const int sx0 = cur.strip * kStrip;
+      const bool fast =
+          cur.n == kRows && a.pair_ok && !a.clamp && sx0 + kStrip <= W &&
+          (!a.valid || (cur.t >= HALO && cur.t + kRows <= static_cast<int>(g.H) - HALO &&
+                        sx0 >= HALO && sx0 + kStrip <= W - HALO));
       float step_sum = 0.f;
+      if (fast) {
 #pragma unroll
-      for (int k = 0; k < kRPT; ++k) {
-        const int row = r0 + k;
-        if (row < cur.n) {
-          const bool row_ok = row >= rlo && row < rhi;
-          const float2 mu1 = res[0][k], mu2 = res[2][k];
-          const float2 mu1_sq = mul2(mu1, mu1), mu2_sq = mul2(mu2, mu2);
-          const float2 msq = add2(mu1_sq, mu2_sq);
-          const float2 mu12 = mul2(mu1, mu2);
-          const float2 A = add2(msq, C1v);
-          float2 B, sigma12;
-          // differences as fma(b, -1, a): the same single rounding as a - b
-          if constexpr (MERGED) {
-            B = add2(fma2(msq, neg1, res[1][k]), C2v);
-            sigma12 = fma2(mu12, neg1, res[3][k]);
-          } else {
-            const float2 sigma1_sq = fma2(mu1_sq, neg1, res[1][k]);
-            const float2 sigma2_sq = fma2(mu2_sq, neg1, res[3][k]);
-            B = add2(add2(sigma1_sq, sigma2_sq), C2v);
-            sigma12 = fma2(mu12, neg1, res[NM - 1][k]);
-          }
-          const float2 Cc = fma2(two, mu12, C1v);
-          const float2 D = fma2(two, sigma12, C2v);
-          const float2 rA = make_float2(rcp_approx(A.x), rcp_approx(A.y));
-          const float2 rB = make_float2(rcp_approx(B.x), rcp_approx(B.y));
-          const float2 rAB = mul2(rA, rB);
-          const float2 v = mul2(mul2(Cc, D), rAB);
-          const bool c0 = row_ok && col0, c1 = row_ok && col1;
-          if (a.reduce) {
-            const float v0 = (a.clamp && v.x < 0.f) ? 0.f : v.x;
-            const float v1 = (a.clamp && v.y < 0.f) ? 0.f : v.y;
-            step_sum += (c0 ? v0 : 0.f) + (c1 ? v1 : 0.f);
-          }
+        for (int k = 0; k < kRPT; ++k) {
+          float2 v, pm, ps, pc;
+          pixel(k, v, pm, ps, pc);
+          if (a.reduce) step_sum += v.x + v.y;
           const int off = off0 + k * W;
-          if (mapp) store2(mapp, off, v, pair, in0, in1);
+          if (mapp) store2(mapp, off, v, true, true, true);
           if (TRAIN) {
-            const bool live0 = !a.mask_partials || (c0 && (!a.clamp || v.x >= 0.f));
-            const bool live1 = !a.mask_partials || (c1 && (!a.clamp || v.y >= 0.f));
-            // dm/dmu1 = 2 mu2 (D - C) / (AB) + 2 mu1 v (1/B - 1/A); dm/dsigma1^2 = -v / B;
-            // dm/dsigma12 = 2 C / (AB)   (csrc/ssim.cu:323-330, with v = CD/(AB))
-            float2 pm = fma2(mul2(two, mu2), mul2(fma2(Cc, neg1, D), rAB),
-                             mul2(mul2(two, mu1), mul2(v, fma2(rA, neg1, rB))));
-            float2 ps = mul2(mul2(v, neg1), rB);
-            float2 pc = mul2(mul2(two, Cc), rAB);
-            if (!live0) pm.x = ps.x = pc.x = 0.f;
-            if (!live1) pm.y = ps.y = pc.y = 0.f;
-            store2(q0, off, pm, pair, in0, in1);
-            store2(q1, off, ps, pair, in0, in1);
-            store2(q2, off, pc, pair, in0, in1);
+            store2(q0, off, pm, true, true, true);
+            store2(q1, off, ps, true, true, true);
+            store2(q2, off, pc, true, true, true);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < kRPT; ++k) {
+          const int row = r0 + k;
+          if (row < cur.n) {
+            const bool row_ok = row >= rlo && row < rhi;
+            float2 v, pm, ps, pc;
+            pixel(k, v, pm, ps, pc);
+            const bool c0 = row_ok && col0, c1 = row_ok && col1;
+            if (a.reduce) {
+              const float v0 = (a.clamp && v.x < 0.f) ? 0.f : v.x;
+              const float v1 = (a.clamp && v.y < 0.f) ? 0.f : v.y;
+              step_sum += (c0 ? v0 : 0.f) + (c1 ? v1 : 0.f);
+            }
+            const int off = off0 + k * W;
+            if (mapp) store2(mapp, off, v, pair, in0, in1);
+            if (TRAIN) {
+              const bool live0 = !a.mask_partials || (c0 && (!a.clamp || v.x >= 0.f));
+              const bool live1 = !a.mask_partials || (c1 && (!a.clamp || v.y >= 0.f));
+              if (!live0) pm.x = ps.x = pc.x = 0.f;
+              if (!live1) pm.y = ps.y = pc.y = 0.f;
+              store2(q0, off, pm, pair, in0, in1);
+              store2(q1, off, ps, pair, in0, in1);
+              store2(q2, off, pc, pair, in0, in1);
+            }
           }
         }
       }
@@ -715,6 +877,7 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
 // Backward kernel
 // ---------------------------------------------------------------------------------------
 struct BwdParams {
+  CUtensorMap tmap[4];    // p0, p1, p2 (TP) and dl (FP32) as (W, H, planes) (when use_tma)
   const void* img1;
   const void* img2;
   const void* p0;         // partials (TP)
@@ -725,21 +888,24 @@ struct BwdParams {
   void* grad;             // output
   Geometry g;
   float chain_scale;
-  int grad_per_image, grad_dtype, aligned16, pair_ok;
+  int grad_per_image, grad_dtype, aligned16, pair_ok, use_tma;
 };
 
 template <int HALO, typename TIn, typename TP, bool DLMAP>
 struct BwdConfig {
   static constexpr bool kHalfW = sizeof(TIn) == 2;
   static constexpr int kMaxR = MaxRows<HALO>::value;
+  static constexpr int kSRows = StageRows<HALO>::value;
   static constexpr int kSP = StagePitch<TP>::value;
   static constexpr int kRP = RingPitch<3>::value;
-  static constexpr size_t kStageBytes = 3ull * kMaxR * kSP * sizeof(TP);
+  static constexpr size_t kStageBytes = 3ull * kSRows * kSP * sizeof(TP);
   static constexpr size_t kDlBytes =
-      DLMAP ? static_cast<size_t>(kMaxR) * StagePitch<float>::value * sizeof(float) : 0;
+      DLMAP ? static_cast<size_t>(kSRows) * StagePitch<float>::value * sizeof(float) : 0;
   static constexpr size_t kRingBytes = static_cast<size_t>(kMaxR) * kRP * sizeof(float);
-  static constexpr size_t kSmem = kStageBytes + kDlBytes + kRingBytes;
-  static constexpr int kMinBlocks = (kSmem + 1024) * 3 <= 228 * 1024 ? 3 : 2;
+  // + 128: the dynamic shared memory base is rounded up to 128 bytes for the TMA boxes
+  static constexpr size_t kSmem = kStageBytes + kDlBytes + kRingBytes + 128;
+  static constexpr int kFit = static_cast<int>((228 * 1024) / (kSmem + 1024));
+  static constexpr int kMinBlocks = kFit >= 4 ? 4 : (kFit >= 3 ? 3 : 2);
 };
 
 // Horizontal pass of the backward over the three partial maps (times dL/dmap on the
@@ -755,12 +921,14 @@ __device__ __forceinline__ void bwd_hpass(const TP* sp, const float* sdl, float*
   // staged layout (same pitch, same aligned left extent HA).
   static_assert(!DLMAP || sizeof(TP) == 4, "per-pixel dL/dmap needs FP32 partials");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int rg = 0; rg < nh; rg += 32) {
-    const int i = rg + lane;
+  // one task (row i, columns 8j..8j+7) per thread per group of kRows rows: lanes 0-15 and
+  // 16-31 of a warp take the same 16 rows in two column chunks
+  static_assert(kRows == 16, "task mapping assumes 16-row steps");
+  for (int rg = 0; rg < nh; rg += kRows) {
+    const int i = rg + (lane & (kRows - 1));
     if (i < nh) {
-#pragma unroll 1
-      for (int jj = 0; jj < 2; ++jj) {
-        const int j = warp + 4 * jj;
+      {
+        const int j = warp + 4 * (lane >> 4);
         float dl[NV];
         if (DLMAP) load_vec(sdl + i * StagePitch<float>::value + 8 * j + kLeft - HA, dl);
         float* dst = ring + (hdst + i) * RP + 8 * j;
@@ -795,15 +963,17 @@ __device__ __forceinline__ void bwd_hpass(const TP* sp, const float* sdl, float*
 
 template <int HALO, typename TIn, typename TP, bool DLMAP>
 __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kMinBlocks))
-    ssim_bwd_kernel(const BwdParams a) {
+    ssim_bwd_kernel(const __grid_constant__ BwdParams a) {
   using Cfg = BwdConfig<HALO, TIn, TP, DLMAP>;
-  constexpr int MAXR = Cfg::kMaxR;
+  constexpr int SROWS = Cfg::kSRows;
   constexpr int RP = Cfg::kRP;
   constexpr bool HW_ = Cfg::kHalfW;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  TP* stg = reinterpret_cast<TP*>(smem_raw);
-  float* sdl = reinterpret_cast<float*>(smem_raw + Cfg::kStageBytes);
-  float* ring = reinterpret_cast<float*>(smem_raw + Cfg::kStageBytes + Cfg::kDlBytes);
+  unsigned char* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
+  TP* stg = reinterpret_cast<TP*>(smem);
+  float* sdl = reinterpret_cast<float*>(smem + Cfg::kStageBytes);
+  float* ring = reinterpret_cast<float*>(smem + Cfg::kStageBytes + Cfg::kDlBytes);
+  __shared__ uint64_t bar;
 
   const Geometry& g = a.g;
   const int64_t beg = (g.LT * blockIdx.x) / gridDim.x;
@@ -819,44 +989,90 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
   Taps2<HALO, HW_> T;
   T.load();
 
+  const bool tma = a.use_tma != 0;
+  if (tma && threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
   Step cur = first_step<HALO>(beg, end, g);
   if (cur.n) {
-    stage<TP, 3, MAXR>(stg, src, g, cur, a.aligned16);
-    if (DLMAP) stage<float, 1, MAXR>(sdl, dsrc, g, cur, a.aligned16);
+    if (!tma) {
+      stage<TP, 3, SROWS>(stg, src, g, cur, a.aligned16);
+      if (DLMAP) stage<float, 1, SROWS>(sdl, dsrc, g, cur, a.aligned16);
+    } else if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(cur.nh) +
+                                      (DLMAP ? tma_step_bytes<float, 1>(cur.nh) : 0u));
+      stage_tma<TP, 3, SROWS>(stg, a.tmap, cur, &bar);
+      if (DLMAP) stage_tma<float, 1, SROWS>(sdl, a.tmap + 3, cur, &bar);
+    }
   }
+  unsigned phase = 0;
   while (cur.n) {
-    cp_async_wait_all();
-    __syncthreads();
-    bwd_hpass<HALO, TIn, TP, DLMAP, MAXR>(stg, sdl, ring, cur.nh, cur.hdst, T);
+    bool timed_out = false;
+    if (tma) {
+      timed_out = !mbar_wait_bounded(&bar, phase);
+      phase ^= 1u;
+    } else {
+      cp_async_wait_all();
+    }
+    if (__syncthreads_or(timed_out)) {
+      // staging did not complete: report it, give the copies in flight one more bounded
+      // wait so none lands after the CTA has exited, and leave
+      if (threadIdx.x == 0) atomicOr(&g_device_error, kErrStagingTimeout);
+      mbar_wait_bounded(&bar, phase ^ 1u);
+      return;
+    }
+    // This step's epilogue operands: the image pairs of the thread's output pixels. The
+    // loads are issued before the H-pass, so they are in flight while both passes run.
+    const int W = static_cast<int>(g.W);
+    const int gx0 = cur.strip * kStrip + 2 * lane;
+    const bool in0 = gx0 < W, in1 = gx0 + 1 < W;
+    const bool pair = a.pair_ok && in1;
+    // a full step of a strip inside the image: no masks, pair loads and stores
+    const bool fast = cur.n == kRows && a.pair_ok && cur.strip * kStrip + kStrip <= W;
+    const int64_t plane_off = cur.plane * g.HW;
+    // plane base + 32-bit in-plane offsets (planes < 2^31 elements)
+    const int off0 = (cur.t + r0) * W + gx0;
+    float2 xin[kRPT], yin[kRPT];
+    {
+      const TIn* x_pl = img1 + plane_off;
+      const TIn* y_pl = img2 + plane_off;
+      if (fast) {
+#pragma unroll
+        for (int k = 0; k < kRPT; ++k) {
+          xin[k] = load2(x_pl, off0 + k * W, true, true, true);
+          yin[k] = load2(y_pl, off0 + k * W, true, true, true);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < kRPT; ++k) {
+          xin[k] = make_float2(0.f, 0.f);
+          yin[k] = xin[k];
+          if (r0 + k < cur.n) {
+            xin[k] = load2(x_pl, off0 + k * W, pair, in0, in1);
+            yin[k] = load2(y_pl, off0 + k * W, pair, in0, in1);
+          }
+        }
+      }
+    }
+    bwd_hpass<HALO, TIn, TP, DLMAP, SROWS>(stg, sdl, ring, cur.nh, cur.hdst, T);
     __syncthreads();
     const Step nxt = next_step<HALO>(cur, g);
     if (nxt.n) {
-      stage<TP, 3, MAXR>(stg, src, g, nxt, a.aligned16);
-      if (DLMAP) stage<float, 1, MAXR>(sdl, dsrc, g, nxt, a.aligned16);
+      if (!tma) {
+        stage<TP, 3, SROWS>(stg, src, g, nxt, a.aligned16);
+        if (DLMAP) stage<float, 1, SROWS>(sdl, dsrc, g, nxt, a.aligned16);
+      } else if (threadIdx.x == 0) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(nxt.nh) +
+                                        (DLMAP ? tma_step_bytes<float, 1>(nxt.nh) : 0u));
+        stage_tma<TP, 3, SROWS>(stg, a.tmap, nxt, &bar);
+        if (DLMAP) stage_tma<float, 1, SROWS>(sdl, a.tmap + 3, nxt, &bar);
+      }
     }
 
     if (r0 < cur.n) {
-      const int gx0 = cur.strip * kStrip + 2 * lane;
-      const int W = static_cast<int>(g.W);
-      const bool in0 = gx0 < W, in1 = gx0 + 1 < W;
-      const bool pair = a.pair_ok && in1;
-      const int64_t plane_off = cur.plane * g.HW;
-      // Issue the epilogue's image loads before the vertical pass so they are in flight
-      // while it runs.
-      // plane base + 32-bit in-plane offsets (planes < 2^31 elements)
-      const int off0 = (cur.t + r0) * W + gx0;
-      const TIn* x_pl = img1 + plane_off;
-      const TIn* y_pl = img2 + plane_off;
-      float2 xin[kRPT], yin[kRPT];
-#pragma unroll
-      for (int k = 0; k < kRPT; ++k) {
-        xin[k] = make_float2(0.f, 0.f);
-        yin[k] = xin[k];
-        if (r0 + k < cur.n) {
-          xin[k] = load2(x_pl, off0 + k * W, pair, in0, in1);
-          yin[k] = load2(y_pl, off0 + k * W, pair, in0, in1);
-        }
-      }
       float2 chain = splat(a.chain_scale);
       if (!DLMAP && a.grad_out) {
         chain = mul2(chain, splat(a.grad_out[a.grad_per_image ? cur.img : 0]));
@@ -870,21 +1086,29 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
           v[q] = *reinterpret_cast<const float2*>(ring + (r0 + q) * RP + m * kStrip + 2 * lane);
         vsumR<HALO, HW_>(v, res[m], T);
       }
+      float2 gv[kRPT];
 #pragma unroll
       for (int k = 0; k < kRPT; ++k) {
-        const int row = r0 + k;
-        if (row < cur.n) {
-          const int off = off0 + k * W;
-          float2 gv = fma2(yin[k], res[2][k], fma2(mul2(two, xin[k]), res[1][k], res[0][k]));
-          if (!DLMAP) gv = mul2(gv, chain);
-          if (a.grad_dtype == 0)
-            store2(static_cast<float*>(a.grad) + plane_off, off, gv, pair, in0, in1);
-          else if (a.grad_dtype == 1)
-            store2(static_cast<__half*>(a.grad) + plane_off, off, gv, pair, in0, in1);
-          else
-            store2(static_cast<__nv_bfloat16*>(a.grad) + plane_off, off, gv, pair, in0, in1);
-        }
+        gv[k] = fma2(yin[k], res[2][k], fma2(mul2(two, xin[k]), res[1][k], res[0][k]));
+        if (!DLMAP) gv[k] = mul2(gv[k], chain);
       }
+      auto store_grad = [&](auto* base) {
+        auto* gp = base + plane_off;
+        if (fast) {
+#pragma unroll
+          for (int k = 0; k < kRPT; ++k) store2(gp, off0 + k * W, gv[k], true, true, true);
+        } else {
+#pragma unroll
+          for (int k = 0; k < kRPT; ++k)
+            if (r0 + k < cur.n) store2(gp, off0 + k * W, gv[k], pair, in0, in1);
+        }
+      };
+      if (a.grad_dtype == 0)
+        store_grad(static_cast<float*>(a.grad));
+      else if (a.grad_dtype == 1)
+        store_grad(static_cast<__half*>(a.grad));
+      else
+        store_grad(static_cast<__nv_bfloat16*>(a.grad));
     }
     __syncthreads();
     if (!cur.last) ring_carry<HALO, RP>(ring);

@@ -60,6 +60,12 @@ const char* fssim_last_error(void);
 /* Library version, e.g. "0.1.0". */
 const char* fssim_version(void);
 
+/* Failures detected inside the kernels on the current device since the flag was last
+ * cleared, as a bit set (0 = none). Bit 0: a kernel's input staging did not complete within
+ * its bounded wait; that kernel left its outputs incomplete (and, for fssim_forward, its
+ * workspace not zero-filled). Synchronises with the device. clear != 0 resets the flag. */
+int fssim_poll_device_error(unsigned* code, int clear);
+
 /* ------------------------------------------------------------------------------------
  * 1. Reference extension functions (map-producing compat seam)
  * ------------------------------------------------------------------------------------ */

@@ -105,3 +105,12 @@ def test_noalloc_rejects_oversized_batch(lib):
     st = lib.fssim_forward_noalloc(ctypes.byref(args), None)
     assert st == 5  # FSSIM_ERR_WORKSPACE
     assert b"at most 4096 images" in lib.fssim_last_error()
+
+
+def test_no_device_side_failures_recorded(lib):
+    """After every GPU test of the session, no kernel has reported a staging timeout."""
+    lib.fssim_poll_device_error.argtypes = [ctypes.POINTER(ctypes.c_uint), ctypes.c_int]
+    lib.fssim_poll_device_error.restype = ctypes.c_int
+    code = ctypes.c_uint(123)
+    assert lib.fssim_poll_device_error(ctypes.byref(code), 0) == 0, lib.fssim_last_error().decode()
+    assert code.value == 0
