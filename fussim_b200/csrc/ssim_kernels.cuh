@@ -62,10 +62,21 @@ template <int NMAP> struct RingPitch { static constexpr int value = NMAP * kStri
 
 template <int HALO> struct MaxRows { static constexpr int value = kRows + 2 * HALO; };
 
-// Staged rows per map: MaxRows rounded up to whole TMA boxes of 8 rows. The map stride
-// (rows x pitch x element size) is then a multiple of 128 bytes, as is every box start.
+// H-pass task mapping. A task is (staged row i, output columns 8j..8j+7), j = 0..7; a group
+// of kRG rows has 8*kRG tasks, one per thread per chunk iteration: lane l of warp w takes
+// row l % kRG of the group and chunks j = w + 4*(l / kRG) + 4*kLG*jj, jj < kJJ.
+constexpr int kRG = kRows < 32 ? kRows : 32;  // rows per group
+constexpr int kLG = 32 / kRG;                 // lane groups per warp (1 or 2)
+constexpr int kJJ = 2 / kLG;                  // chunk iterations per thread per group
+static_assert(kRows == 16 || kRows == 32, "steps of 16 or 32 rows");
+
+// Staged rows per map: MaxRows rounded up to whole TMA boxes of 8 rows, and at least two
+// slots of kRows rows, so a step can be staged into one slot while the H-pass reads the
+// other. The map stride (rows x pitch x element size) is then a multiple of 128 bytes, as
+// is every box start.
 template <int HALO> struct StageRows {
-  static constexpr int value = (MaxRows<HALO>::value + 7) / 8 * 8;
+  static constexpr int kBoxed = (MaxRows<HALO>::value + 7) / 8 * 8;
+  static constexpr int value = kBoxed > 2 * kRows ? kBoxed : 2 * kRows;
 };
 
 // Gaussian taps: [half-rounded][halo-3][k], k = 0..2*HALO, symmetric.
@@ -336,7 +347,8 @@ struct Step {
   int n;          // output rows in this step (1..kRows); 0 = no step
   int h0;         // first moment row computed by this step
   int nh;         // moment rows computed by this step
-  int hdst;       // ring row receiving moment row h0
+  int hdst;       // ring row receiving moment row h0 (0 for the first step of a run)
+  int slot;       // first staging row of the step (0 or kRows)
   bool last;      // last step of its column run
 };
 
@@ -371,6 +383,7 @@ __device__ __forceinline__ Step first_step(int64_t beg, int64_t end, const Geome
   s.strip = static_cast<int>(col - s.plane * g.S);
   s.img = static_cast<int>(s.plane / g.C);
   s.chan = static_cast<int>(s.plane - static_cast<int64_t>(s.img) * g.C);
+  s.slot = 0;
   fill_step<HALO>(s, true, g);
   return s;
 }
@@ -476,7 +489,8 @@ __device__ __forceinline__ unsigned tma_step_bytes(int nh) {
 
 // TMA staging of one step, issued by a single thread: rows [h0, h0+nh) rounded up to whole
 // boxes, columns [x0-8, x0-8+pitch) of plane s.plane for each of the NMAP tensor maps, into
-// the layout [NMAP][SROWS][pitch]. Rows or columns outside the image arrive as zeros.
+// rows [slot, slot + nh) of the layout [NMAP][SROWS][pitch]. Rows or columns outside the
+// image arrive as zeros.
 template <typename T, int NMAP, int SROWS>
 __device__ __forceinline__ void stage_tma(T* sm, const CUtensorMap* maps, const Step& s,
                                           uint64_t* bar) {
@@ -487,7 +501,8 @@ __device__ __forceinline__ void stage_tma(T* sm, const CUtensorMap* maps, const 
 #pragma unroll
   for (int m = 0; m < NMAP; ++m)
     for (int b = 0; b < nbox; ++b)
-      tma_load_3d(sm + (m * SROWS + b * kBoxRows) * P, maps + m, x0, s.h0 + b * kBoxRows, z, bar);
+      tma_load_3d(sm + (m * SROWS + s.slot + b * kBoxRows) * P, maps + m, x0,
+                  s.h0 + b * kBoxRows, z, bar);
 }
 
 // Copy ring rows [kRows, kRows + 2*HALO) to [0, 2*HALO): the vertical halo for the next
@@ -588,14 +603,12 @@ __device__ __forceinline__ void fwd_hpass(const TIn* sx, const TIn* sy, float* r
   constexpr int HA = (sizeof(TIn) == 2 || HALO > 4) ? 8 : 4;  // aligned left extent
   constexpr int NV = 8 + 2 * HA;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // one task (row i, columns 8j..8j+7) per thread per group of kRows rows: lanes 0-15 and
-  // 16-31 of a warp take the same 16 rows in two column chunks
-  static_assert(kRows == 16, "task mapping assumes 16-row steps");
-  for (int rg = 0; rg < nh; rg += kRows) {
-    const int i = rg + (lane & (kRows - 1));
+  for (int rg = 0; rg < nh; rg += kRG) {
+    const int i = rg + lane % kRG;
     if (i < nh) {
-      {
-        const int j = warp + 4 * (lane >> 4);
+#pragma unroll 1
+      for (int jj = 0; jj < kJJ; ++jj) {
+        const int j = warp + 4 * (lane / kRG) + 4 * kLG * jj;
         float xv[NV], yv[NV];
         load_vec(sx + i * SP + 8 * j + kLeft - HA, xv);
         load_vec(sy + i * SP + 8 * j + kLeft - HA, yv);
@@ -704,10 +717,21 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
       mbar_wait_bounded(&bar, phase ^ 1u);
       return;
     }
-    fwd_hpass<HALO, TIn, SROWS, MERGED>(stg, stg + SROWS * SP, ring, cur.nh, cur.hdst, T);
+    // The next step is staged into the other slot while this step's H-pass runs, unless
+    // one of the two is the first step of a column run (which fills both slots); then it
+    // is staged after the H-pass.
+    Step nxt = next_step<HALO>(cur, g);
+    const bool early = tma && nxt.n && cur.hdst != 0 && nxt.hdst != 0;
+    nxt.slot = early ? (cur.slot ^ kRows) : 0;
+    if (early && threadIdx.x == 0) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(nxt.nh));
+      stage_tma<TIn, 2, SROWS>(stg, a.tmap, nxt, &bar);
+    }
+    fwd_hpass<HALO, TIn, SROWS, MERGED>(stg + cur.slot * SP, stg + (SROWS + cur.slot) * SP, ring,
+                                        cur.nh, cur.hdst, T);
     __syncthreads();
-    const Step nxt = next_step<HALO>(cur, g);
-    if (nxt.n) {
+    if (nxt.n && !early) {
       if (!tma) {
         stage<TIn, 2, SROWS>(stg, src, g, nxt, a.aligned16);
       } else if (threadIdx.x == 0) {
@@ -921,14 +945,12 @@ __device__ __forceinline__ void bwd_hpass(const TP* sp, const float* sdl, float*
   // staged layout (same pitch, same aligned left extent HA).
   static_assert(!DLMAP || sizeof(TP) == 4, "per-pixel dL/dmap needs FP32 partials");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // one task (row i, columns 8j..8j+7) per thread per group of kRows rows: lanes 0-15 and
-  // 16-31 of a warp take the same 16 rows in two column chunks
-  static_assert(kRows == 16, "task mapping assumes 16-row steps");
-  for (int rg = 0; rg < nh; rg += kRows) {
-    const int i = rg + (lane & (kRows - 1));
+  for (int rg = 0; rg < nh; rg += kRG) {
+    const int i = rg + lane % kRG;
     if (i < nh) {
-      {
-        const int j = warp + 4 * (lane >> 4);
+#pragma unroll 1
+      for (int jj = 0; jj < kJJ; ++jj) {
+        const int j = warp + 4 * (lane / kRG) + 4 * kLG * jj;
         float dl[NV];
         if (DLMAP) load_vec(sdl + i * StagePitch<float>::value + 8 * j + kLeft - HA, dl);
         float* dst = ring + (hdst + i) * RP + 8 * j;
@@ -1056,10 +1078,22 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
         }
       }
     }
-    bwd_hpass<HALO, TIn, TP, DLMAP, SROWS>(stg, sdl, ring, cur.nh, cur.hdst, T);
+    // next step staged into the other slot during the H-pass (see the forward kernel)
+    Step nxt = next_step<HALO>(cur, g);
+    const bool early = tma && nxt.n && cur.hdst != 0 && nxt.hdst != 0;
+    nxt.slot = early ? (cur.slot ^ kRows) : 0;
+    if (early && threadIdx.x == 0) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(nxt.nh) +
+                                      (DLMAP ? tma_step_bytes<float, 1>(nxt.nh) : 0u));
+      stage_tma<TP, 3, SROWS>(stg, a.tmap, nxt, &bar);
+      if (DLMAP) stage_tma<float, 1, SROWS>(sdl, a.tmap + 3, nxt, &bar);
+    }
+    bwd_hpass<HALO, TIn, TP, DLMAP, SROWS>(stg + cur.slot * Cfg::kSP,
+                                           sdl + cur.slot * StagePitch<float>::value, ring,
+                                           cur.nh, cur.hdst, T);
     __syncthreads();
-    const Step nxt = next_step<HALO>(cur, g);
-    if (nxt.n) {
+    if (nxt.n && !early) {
       if (!tma) {
         stage<TP, 3, SROWS>(stg, src, g, nxt, a.aligned16);
         if (DLMAP) stage<float, 1, SROWS>(sdl, dsrc, g, nxt, a.aligned16);
