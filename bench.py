@@ -50,6 +50,11 @@ BWD_BYTES_F32 = 12 + 8 + 4    # read 3 partials, img1, img2; write grad
 FWD_FLOPS = 2 * 5 * 2 * 11 + 3 + 30   # 5 moments x 2 passes x 11 MACs, 3 products, epilogue
 BWD_FLOPS = 2 * 3 * 2 * 11 + 6        # 3 partial maps x 2 passes x 11 MACs, combine + chain
 
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each kernel on
+# this workload, from one ncu capture (profiles/ssim_fwd_bwd_1080p_fp32.md; the capture
+# flushes L2 before each launch, so it is the cold-L2 figure).
+NCU_TRAFFIC_BYTES = {"fwd": 61.06e6 + 28.30e6, "bwd": 175.63e6 + 15.76e6}
+
 
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -327,7 +332,9 @@ def measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, step_ms
     else:
         roof = {"bound": "fp32", "achieved": d["tflops"], "peak": fp32_peak, "unit": "TFLOP/s",
                 "frac": d["tflops"] / fp32_peak, "traffic": None}
-    roof.update(kernel=f"ssim_{dom}_kernel", launch_us=d["us"],
+    roof["traffic"] = NCU_TRAFFIC_BYTES[dom]
+    roof.update(kernel=f"ssim_{dom}_kernel", launch_us=d["us"], traffic_unit="bytes per launch",
+                algorithmic_bytes=d["bytes"],
                 peak_source=("hbm: MEASURED_PEAKS.json (measured)" if peaks["source"] == "measured"
                              else "hbm: fallback") + "; fp32: 148 SMs x 128 lanes x 2 x sm_max_mhz")
     out["roofline"] = roof
