@@ -42,6 +42,8 @@ int check_shape(int64_t B, int64_t C, int64_t H, int64_t W) {
     return fail(FSSIM_ERR_SHAPE, "dimension too large (H, W must be < 2^30)");
   if (H * W > static_cast<int64_t>(INT_MAX))
     return fail(FSSIM_ERR_SHAPE, "H*W must be < 2^31 elements per image plane");
+  if (B * C > static_cast<int64_t>(INT_MAX))
+    return fail(FSSIM_ERR_SHAPE, "B*C must be < 2^31 image planes");
   const double n = static_cast<double>(B) * C * H * W;
   if (n > 4.0e18) return fail(FSSIM_ERR_SHAPE, "B*C*H*W overflows int64");
   return FSSIM_OK;
@@ -186,6 +188,7 @@ int launch_fwd(const fssim::FwdParams& p, cudaStream_t stream) {
   st = device_sms(&sms);
   if (st) return st;
   const int grid = grid_size(p.g, occ, sms);
+  if ((p.g.LT + grid - 1) / grid > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
   k<<<grid, fssim::kThreads, Cfg::kSmem, stream>>>(p);
   return launch_error("ssim forward launch");
 }
@@ -202,6 +205,7 @@ int launch_bwd(const fssim::BwdParams& p, cudaStream_t stream) {
   st = device_sms(&sms);
   if (st) return st;
   const int grid = grid_size(p.g, occ, sms);
+  if ((p.g.LT + grid - 1) / grid > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
   k<<<grid, fssim::kThreads, Cfg::kSmem, stream>>>(p);
   return launch_error("ssim backward launch");
 }

@@ -335,72 +335,63 @@ struct Geometry {
   int B;             // images
 };
 
-// Position of a CTA in its range: the column run (plane, strip) and row of the next step.
-// Advanced incrementally, so a step costs no 64-bit divisions.
+// Position of a CTA in its range: the column run (plane, strip), the part of it that
+// belongs to the CTA (rows up to t_end) and the next step. 32-bit throughout (the host
+// keeps planes and per-CTA ranges below 2^31) and advanced incrementally, so a step costs
+// a handful of integer operations.
+template <int HALO>
 struct Step {
-  int64_t left;   // strip-rows of the CTA's range not yet processed (including this step)
-  int64_t plane;
-  int img;        // image of the plane (plane / C), tracked alongside
-  int chan;       // channel of the plane (plane % C)
+  int plane;      // plane of the current column run (image img, channel chan)
+  int img, chan;
   int strip;
   int t;          // first output row of this step
   int n;          // output rows in this step (1..kRows); 0 = no step
-  int h0;         // first moment row computed by this step
-  int nh;         // moment rows computed by this step
-  int hdst;       // ring row receiving moment row h0 (0 for the first step of a run)
+  int t_end;      // end row of the CTA's part of this column run
+  int rest;       // strip-rows of the CTA's range after that part
   int slot;       // first staging row of the step (0 or kRows)
-  bool last;      // last step of its column run
+  bool first;     // first step of a run part: it also computes the top halo rows
+  __device__ __forceinline__ int h0() const { return first ? t - HALO : t + HALO; }  // first moment row
+  __device__ __forceinline__ int nh() const { return first ? n + 2 * HALO : n; }     // moment rows
+  __device__ __forceinline__ int hdst() const { return first ? 0 : 2 * HALO; }       // ring row of h0
+  __device__ __forceinline__ bool last() const { return t + n == t_end; }  // last step of the part
 };
 
 template <int HALO>
-__device__ __forceinline__ void fill_step(Step& s, bool first, const Geometry& g) {
-  const int rows_left_in_run = static_cast<int>(g.H) - s.t;
-  const int run = s.left < rows_left_in_run ? static_cast<int>(s.left) : rows_left_in_run;
-  s.n = run < kRows ? run : kRows;
-  s.last = (s.n == run);
-  if (first) {
-    s.h0 = s.t - HALO;
-    s.nh = s.n + 2 * HALO;
-    s.hdst = 0;
-  } else {
-    s.h0 = s.t + HALO;
-    s.nh = s.n;
-    s.hdst = 2 * HALO;
-  }
-}
-
-template <int HALO>
-__device__ __forceinline__ Step first_step(int64_t beg, int64_t end, const Geometry& g) {
-  Step s;
-  s.left = end - beg;
-  if (s.left <= 0) {
+__device__ __forceinline__ Step<HALO> first_step(int64_t beg, int64_t end, const Geometry& g) {
+  Step<HALO> s;
+  const int64_t len = end - beg;
+  if (len <= 0) {
     s.n = 0;
     return s;
   }
   const int64_t col = beg / g.H;
   s.t = static_cast<int>(beg - col * g.H);
-  s.plane = col / g.S;
-  s.strip = static_cast<int>(col - s.plane * g.S);
-  s.img = static_cast<int>(s.plane / g.C);
-  s.chan = static_cast<int>(s.plane - static_cast<int64_t>(s.img) * g.C);
+  const int64_t plane = col / g.S;
+  s.plane = static_cast<int>(plane);
+  s.strip = static_cast<int>(col - plane * g.S);
+  s.img = s.plane / g.C;
+  s.chan = s.plane - s.img * g.C;
+  const int64_t seg = (g.H - s.t) < len ? (g.H - s.t) : len;
+  s.t_end = s.t + static_cast<int>(seg);
+  s.rest = static_cast<int>(len - seg);
   s.slot = 0;
-  fill_step<HALO>(s, true, g);
+  s.first = true;
+  s.n = static_cast<int>(seg) < kRows ? static_cast<int>(seg) : kRows;
   return s;
 }
 
 template <int HALO>
-__device__ __forceinline__ Step next_step(const Step& c, const Geometry& g) {
-  Step s = c;
-  s.left = c.left - c.n;
-  if (s.left <= 0) {
-    s.n = 0;
-    return s;
-  }
-  bool first = false;
+__device__ __forceinline__ Step<HALO> next_step(const Step<HALO>& c, const Geometry& g) {
+  Step<HALO> s = c;
   s.t = c.t + c.n;
-  if (s.t == g.H) {  // next column run
+  s.first = false;
+  if (s.t == c.t_end) {  // the CTA's part of this column run is done
+    if (c.rest == 0) {
+      s.n = 0;
+      return s;
+    }
     s.t = 0;
-    first = true;
+    s.first = true;
     if (++s.strip == g.S) {
       s.strip = 0;
       ++s.plane;
@@ -409,32 +400,38 @@ __device__ __forceinline__ Step next_step(const Step& c, const Geometry& g) {
         ++s.img;
       }
     }
+    const int H = static_cast<int>(g.H);
+    const int seg = c.rest < H ? c.rest : H;
+    s.t_end = seg;
+    s.rest = c.rest - seg;
   }
-  fill_step<HALO>(s, first, g);
+  const int r = s.t_end - s.t;
+  s.n = r < kRows ? r : kRows;
   return s;
 }
 
 // Stage moment rows [h0, h0+nh) x columns [x0-8, x0+72) of NMAP planes into smem
 // (layout [NMAP][MAXR][PITCH]); out-of-image elements become zero.
-template <typename T, int NMAP, int MAXR>
+template <typename T, int NMAP, int MAXR, typename StepT>
 __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const Geometry& g,
-                                      const Step& s, bool aligned16) {
+                                      const StepT& s, bool aligned16) {
   constexpr int P = StagePitch<T>::value;
   const int x0 = s.strip * kStrip - kLeft;
   const int W = static_cast<int>(g.W);
   const int H = static_cast<int>(g.H);
+  const int h0 = s.h0();
   if (aligned16) {
     constexpr int E = 16 / sizeof(T);   // elements per 16-byte chunk
     constexpr int CH = kInCols / E;      // chunks per staged row
-    const int total = s.nh * CH;
+    const int total = s.nh() * CH;
 #pragma unroll
     for (int m = 0; m < NMAP; ++m) {
-      const T* plane = src[m] + s.plane * g.HW;
+      const T* plane = src[m] + static_cast<int64_t>(s.plane) * g.HW;
       T* dst = sm + m * MAXR * P;
       for (int i = threadIdx.x; i < total; i += kThreads) {
         const int row = i / CH;
         const int ch = i - row * CH;
-        const int gy = s.h0 + row;
+        const int gy = h0 + row;
         const int gx = x0 + ch * E;
         const bool in = (static_cast<unsigned>(gy) < static_cast<unsigned>(H)) &&
                         (static_cast<unsigned>(gx) < static_cast<unsigned>(W));
@@ -443,15 +440,15 @@ __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const 
       }
     }
   } else if constexpr (sizeof(T) == 4) {
-    const int total = s.nh * kInCols;
+    const int total = s.nh() * kInCols;
 #pragma unroll
     for (int m = 0; m < NMAP; ++m) {
-      const T* plane = src[m] + s.plane * g.HW;
+      const T* plane = src[m] + static_cast<int64_t>(s.plane) * g.HW;
       T* dst = sm + m * MAXR * P;
       for (int i = threadIdx.x; i < total; i += kThreads) {
         const int row = i / kInCols;
         const int c = i - row * kInCols;
-        const int gy = s.h0 + row;
+        const int gy = h0 + row;
         const int gx = x0 + c;
         const bool in = (static_cast<unsigned>(gy) < static_cast<unsigned>(H)) &&
                         (static_cast<unsigned>(gx) < static_cast<unsigned>(W));
@@ -461,15 +458,15 @@ __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const 
     }
   } else {
     // 2-byte elements on an unaligned layout: plain loads.
-    const int total = s.nh * kInCols;
+    const int total = s.nh() * kInCols;
 #pragma unroll
     for (int m = 0; m < NMAP; ++m) {
-      const T* plane = src[m] + s.plane * g.HW;
+      const T* plane = src[m] + static_cast<int64_t>(s.plane) * g.HW;
       T* dst = sm + m * MAXR * P;
       for (int i = threadIdx.x; i < total; i += kThreads) {
         const int row = i / kInCols;
         const int c = i - row * kInCols;
-        const int gy = s.h0 + row;
+        const int gy = h0 + row;
         const int gx = x0 + c;
         const bool in = (static_cast<unsigned>(gy) < static_cast<unsigned>(H)) &&
                         (static_cast<unsigned>(gx) < static_cast<unsigned>(W));
@@ -491,18 +488,19 @@ __device__ __forceinline__ unsigned tma_step_bytes(int nh) {
 // boxes, columns [x0-8, x0-8+pitch) of plane s.plane for each of the NMAP tensor maps, into
 // rows [slot, slot + nh) of the layout [NMAP][SROWS][pitch]. Rows or columns outside the
 // image arrive as zeros.
-template <typename T, int NMAP, int SROWS>
-__device__ __forceinline__ void stage_tma(T* sm, const CUtensorMap* maps, const Step& s,
+template <typename T, int NMAP, int SROWS, typename StepT>
+__device__ __forceinline__ void stage_tma(T* sm, const CUtensorMap* maps, const StepT& s,
                                           uint64_t* bar) {
   constexpr int P = StagePitch<T>::value;
-  const int nbox = (s.nh + kBoxRows - 1) / kBoxRows;
+  const int nbox = (s.nh() + kBoxRows - 1) / kBoxRows;
   const int x0 = s.strip * kStrip - kLeft;
-  const int z = static_cast<int>(s.plane);
+  const int z = s.plane;
+  const int h0 = s.h0();
 #pragma unroll
   for (int m = 0; m < NMAP; ++m)
     for (int b = 0; b < nbox; ++b)
       tma_load_3d(sm + (m * SROWS + s.slot + b * kBoxRows) * P, maps + m, x0,
-                  s.h0 + b * kBoxRows, z, bar);
+                  h0 + b * kBoxRows, z, bar);
 }
 
 // Copy ring rows [kRows, kRows + 2*HALO) to [0, 2*HALO): the vertical halo for the next
@@ -690,12 +688,12 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
     fence_mbar_init();
   }
   __syncthreads();
-  Step cur = first_step<HALO>(beg, end, g);
+  Step<HALO> cur = first_step<HALO>(beg, end, g);
   if (cur.n) {
     if (!tma) {
       stage<TIn, 2, SROWS>(stg, src, g, cur, a.aligned16);
     } else if (threadIdx.x == 0) {
-      mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(cur.nh));
+      mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(cur.nh()));
       stage_tma<TIn, 2, SROWS>(stg, a.tmap, cur, &bar);
     }
   }
@@ -720,23 +718,23 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
     // The next step is staged into the other slot while this step's H-pass runs, unless
     // one of the two is the first step of a column run (which fills both slots); then it
     // is staged after the H-pass.
-    Step nxt = next_step<HALO>(cur, g);
-    const bool early = tma && nxt.n && cur.hdst != 0 && nxt.hdst != 0;
+    Step<HALO> nxt = next_step<HALO>(cur, g);
+    const bool early = tma && nxt.n && !cur.first && !nxt.first;
     nxt.slot = early ? (cur.slot ^ kRows) : 0;
     if (early && threadIdx.x == 0) {
       fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(nxt.nh));
+      mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(nxt.nh()));
       stage_tma<TIn, 2, SROWS>(stg, a.tmap, nxt, &bar);
     }
     fwd_hpass<HALO, TIn, SROWS, MERGED>(stg + cur.slot * SP, stg + (SROWS + cur.slot) * SP, ring,
-                                        cur.nh, cur.hdst, T);
+                                        cur.nh(), cur.hdst(), T);
     __syncthreads();
     if (nxt.n && !early) {
       if (!tma) {
         stage<TIn, 2, SROWS>(stg, src, g, nxt, a.aligned16);
       } else if (threadIdx.x == 0) {
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(nxt.nh));
+        mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(nxt.nh()));
         stage_tma<TIn, 2, SROWS>(stg, a.tmap, nxt, &bar);
       }
     }
@@ -766,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
         rhi = min(cur.n, static_cast<int>(g.H) - HALO - cur.t);
       }
       // outputs addressed as plane base + 32-bit in-plane offset (planes < 2^31 elements)
-      const int64_t plane_off = cur.plane * g.HW;
+      const int64_t plane_off = static_cast<int64_t>(cur.plane) * g.HW;
       const int off0 = (cur.t + r0) * W + gx0;
       float* mapp = a.map ? a.map + plane_off : nullptr;
       TP* q0 = TRAIN ? static_cast<TP*>(a.p0) + plane_off : nullptr;
@@ -859,7 +857,7 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
       run_sum += static_cast<double>(step_sum);
     }
 
-    if (a.reduce && cur.last) {
+    if (a.reduce && cur.last()) {
       // end of a column run: fold its sum into the image's fixed-point accumulator
       const double s = block_sum(run_sum, red);
       run_sum = 0.0;
@@ -869,7 +867,7 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
       }
     }
     __syncthreads();
-    if (!cur.last) ring_carry<HALO, RP>(ring);
+    if (!cur.last()) ring_carry<HALO, RP>(ring);
     cur = nxt;
   }
 
@@ -1017,14 +1015,14 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
     fence_mbar_init();
   }
   __syncthreads();
-  Step cur = first_step<HALO>(beg, end, g);
+  Step<HALO> cur = first_step<HALO>(beg, end, g);
   if (cur.n) {
     if (!tma) {
       stage<TP, 3, SROWS>(stg, src, g, cur, a.aligned16);
       if (DLMAP) stage<float, 1, SROWS>(sdl, dsrc, g, cur, a.aligned16);
     } else if (threadIdx.x == 0) {
-      mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(cur.nh) +
-                                      (DLMAP ? tma_step_bytes<float, 1>(cur.nh) : 0u));
+      mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(cur.nh()) +
+                                      (DLMAP ? tma_step_bytes<float, 1>(cur.nh()) : 0u));
       stage_tma<TP, 3, SROWS>(stg, a.tmap, cur, &bar);
       if (DLMAP) stage_tma<float, 1, SROWS>(sdl, a.tmap + 3, cur, &bar);
     }
@@ -1053,7 +1051,7 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
     const bool pair = a.pair_ok && in1;
     // a full step of a strip inside the image: no masks, pair loads and stores
     const bool fast = cur.n == kRows && a.pair_ok && cur.strip * kStrip + kStrip <= W;
-    const int64_t plane_off = cur.plane * g.HW;
+    const int64_t plane_off = static_cast<int64_t>(cur.plane) * g.HW;
     // plane base + 32-bit in-plane offsets (planes < 2^31 elements)
     const int off0 = (cur.t + r0) * W + gx0;
     float2 xin[kRPT], yin[kRPT];
@@ -1079,19 +1077,19 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
       }
     }
     // next step staged into the other slot during the H-pass (see the forward kernel)
-    Step nxt = next_step<HALO>(cur, g);
-    const bool early = tma && nxt.n && cur.hdst != 0 && nxt.hdst != 0;
+    Step<HALO> nxt = next_step<HALO>(cur, g);
+    const bool early = tma && nxt.n && !cur.first && !nxt.first;
     nxt.slot = early ? (cur.slot ^ kRows) : 0;
     if (early && threadIdx.x == 0) {
       fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(nxt.nh) +
-                                      (DLMAP ? tma_step_bytes<float, 1>(nxt.nh) : 0u));
+      mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(nxt.nh()) +
+                                      (DLMAP ? tma_step_bytes<float, 1>(nxt.nh()) : 0u));
       stage_tma<TP, 3, SROWS>(stg, a.tmap, nxt, &bar);
       if (DLMAP) stage_tma<float, 1, SROWS>(sdl, a.tmap + 3, nxt, &bar);
     }
     bwd_hpass<HALO, TIn, TP, DLMAP, SROWS>(stg + cur.slot * Cfg::kSP,
                                            sdl + cur.slot * StagePitch<float>::value, ring,
-                                           cur.nh, cur.hdst, T);
+                                           cur.nh(), cur.hdst(), T);
     __syncthreads();
     if (nxt.n && !early) {
       if (!tma) {
@@ -1099,8 +1097,8 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
         if (DLMAP) stage<float, 1, SROWS>(sdl, dsrc, g, nxt, a.aligned16);
       } else if (threadIdx.x == 0) {
         fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(nxt.nh) +
-                                        (DLMAP ? tma_step_bytes<float, 1>(nxt.nh) : 0u));
+        mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(nxt.nh()) +
+                                        (DLMAP ? tma_step_bytes<float, 1>(nxt.nh()) : 0u));
         stage_tma<TP, 3, SROWS>(stg, a.tmap, nxt, &bar);
         if (DLMAP) stage_tma<float, 1, SROWS>(sdl, a.tmap + 3, nxt, &bar);
       }
@@ -1145,7 +1143,7 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
         store_grad(static_cast<__nv_bfloat16*>(a.grad));
     }
     __syncthreads();
-    if (!cur.last) ring_carry<HALO, RP>(ring);
+    if (!cur.last()) ring_carry<HALO, RP>(ring);
     cur = nxt;
   }
 }
