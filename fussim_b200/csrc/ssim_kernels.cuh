@@ -165,7 +165,7 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // bytes, one thread stages a step with a handful of tiled bulk copies (boxes of kBoxRows
 // rows x one staged row pitch of columns, zero-filled outside the image by the copy unit)
 // that complete on an mbarrier. This replaces 2-4 cp.async chunks per thread per staged
-// row and all their address arithmetic. The copies never use cluster multicast.
+// row and all their address arithmetic. Each copy reads this GPU's own memory into this CTA only.
 constexpr int kBoxRows = 8;
 constexpr int kWaitLimit = 1 << 20;  // bounded mbarrier polls before a step reports failure
 
