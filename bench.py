@@ -4,8 +4,9 @@
 Workload (per GPU): the 3DGS training-step shape, 1x3x1080x1920 FP32 render/ground-truth
 pair (seeded synthetic blob field + 3x3 box blur + noise), padding "same", window 11,
 train=True: ``loss = fused_ssim(img1, img2); loss.backward()`` through the public API.
-With N GPUs (torchrun) every rank holds its own 1080p pair (weak scaling) and the global
-mean is formed by one NCCL all-reduce that overlaps the local backward.
+With N GPUs (torchrun) every rank holds its own 1080p pair (weak scaling); the global mean
+is formed by the forward kernels publishing their sums to every rank's mailbox over NVLink
+and a one-warp gather kernel per rank (no collective call in the step).
 
 Reported:
 * value      B*C*H*W/s of all ranks over the max-over-ranks device time (Mpix/s, the
@@ -265,6 +266,7 @@ def main():
     if rank == 0 and not args.skip_extras:
         extras = measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, ms)
     if world > 1:
+        fdist.release_mailboxes()
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <climits>
 #include <cstdint>
 #include <cstdio>
@@ -105,8 +106,14 @@ int kernel_occupancy(Kernel k, size_t smem, int (&cache)[64], std::mutex& mu, in
 }
 
 // Persistent grid: one CTA per resident slot, but no CTA with fewer than ~2 steps of rows.
+// SMs the persistent grids leave free (fssim_set_reserved_sms), e.g. for a collective
+// that runs concurrently with a kernel of this library.
+std::atomic<int> g_reserved_sms{0};
+
 int grid_size(const fssim::Geometry& g, int occ, int sms) {
-  const int64_t slots = static_cast<int64_t>(occ) * sms;
+  int use = sms - g_reserved_sms.load(std::memory_order_relaxed);
+  if (use < 1) use = 1;
+  const int64_t slots = static_cast<int64_t>(occ) * use;
   const int64_t by_work = (g.LT + 2 * fssim::kRows - 1) / (2 * fssim::kRows);
   int64_t grid = slots < by_work ? slots : by_work;
   if (grid < 1) grid = 1;
@@ -331,6 +338,13 @@ const char* fssim_last_error(void) { return g_last_error.c_str(); }
 
 const char* fssim_version(void) { return "0.1.0"; }
 
+int fssim_set_reserved_sms(int n) {
+  g_last_error.clear();
+  if (n < 0) return fail(FSSIM_ERR_ARGUMENT, "reserved SM count must be >= 0");
+  g_reserved_sms.store(n, std::memory_order_relaxed);
+  return FSSIM_OK;
+}
+
 int fssim_poll_device_error(unsigned* code, int clear) {
   g_last_error.clear();
   if (!code) return fail(FSSIM_ERR_NULLPTR, "code is NULL");
@@ -402,8 +416,12 @@ size_t fssim_forward_workspace_bytes(int64_t B) {
   return 256 + static_cast<size_t>(B) * sizeof(unsigned long long);
 }
 
-int fssim_forward(const fssim_forward_args* a, fssim_stream_t stream) {
-  g_last_error.clear();
+}  // extern "C"
+
+namespace {
+
+// fssim_forward, optionally publishing the batch sum to the ranks of a sharded loss.
+int forward_impl(const fssim_forward_args* a, const fssim::DpParams* dp, cudaStream_t stream) {
   if (!a) return fail(FSSIM_ERR_NULLPTR, "args is NULL");
   int st = check_window(a->window_size);
   if (st) return st;
@@ -475,6 +493,7 @@ int fssim_forward(const fssim_forward_args* a, fssim_stream_t stream) {
   if (a->train) pair = pair && aligned(p.p0, 2 * PE) && aligned(p.p1, 2 * PE) && aligned(p.p2, 2 * PE);
   p.pair_ok = pair;
   set_fwd_tma(p, E);
+  if (dp) p.dp = *dp;
 
   const int ws = a->window_size;
   cudaStream_t s = stream;
@@ -485,6 +504,119 @@ int fssim_forward(const fssim_forward_args* a, fssim_stream_t stream) {
   if (!a->train) return dispatch_fwd<__half, float, false, true>(ws, p, s);
   if (a->partial_dtype == FSSIM_F16) return dispatch_fwd<__half, __half, true, true>(ws, p, s);
   return dispatch_fwd<__half, float, true, true>(ws, p, s);
+}
+
+int check_dp(const fssim_dp_args* d, fssim::DpParams* out) {
+  if (!d) return fail(FSSIM_ERR_NULLPTR, "dp args is NULL");
+  if (d->world < 1 || d->world > FSSIM_DP_MAX_RANKS)
+    return fail(FSSIM_ERR_ARGUMENT, "world must be in [1, " + std::to_string(FSSIM_DP_MAX_RANKS) + "]");
+  if (d->rank < 0 || d->rank >= d->world) return fail(FSSIM_ERR_ARGUMENT, "rank out of range");
+  fssim::DpParams p{};
+  for (int r = 0; r < d->world; ++r) {
+    if (!d->mailboxes[r]) return fail(FSSIM_ERR_NULLPTR, "mailbox pointer missing");
+    if (!aligned(d->mailboxes[r], 16)) return fail(FSSIM_ERR_ARGUMENT, "mailbox not 16-byte aligned");
+    p.mail[r] = static_cast<fssim::DpMailSlot*>(d->mailboxes[r]);
+  }
+  p.world = d->world;
+  p.rank = d->rank;
+  p.seq = d->seq;
+  *out = p;
+  return FSSIM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fssim_forward(const fssim_forward_args* a, fssim_stream_t stream) {
+  g_last_error.clear();
+  return forward_impl(a, nullptr, stream);
+}
+
+size_t fssim_dp_mailbox_bytes(int world) {
+  if (world < 1) return 0;
+  return 2 * static_cast<size_t>(world) * sizeof(fssim::DpMailSlot);
+}
+
+int fssim_dp_mailbox_alloc(int world, void** mailbox) {
+  g_last_error.clear();
+  if (!mailbox) return fail(FSSIM_ERR_NULLPTR, "mailbox is NULL");
+  if (world < 1 || world > FSSIM_DP_MAX_RANKS) return fail(FSSIM_ERR_ARGUMENT, "world out of range");
+  void* p = nullptr;
+  // a whole allocation of its own, so its IPC handle maps exactly this buffer
+  cudaError_t e = cudaMalloc(&p, fssim_dp_mailbox_bytes(world));
+  if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string("cudaMalloc(mailbox): ") + cudaGetErrorString(e));
+  // seq 0 is never used by a step, so zero-filled slots hold no message
+  e = cudaMemset(p, 0, fssim_dp_mailbox_bytes(world));
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(FSSIM_ERR_CUDA, std::string("cudaMemset(mailbox): ") + cudaGetErrorString(e));
+  }
+  *mailbox = p;
+  return FSSIM_OK;
+}
+
+int fssim_dp_mailbox_free(void* mailbox) {
+  g_last_error.clear();
+  if (!mailbox) return FSSIM_OK;
+  const cudaError_t e = cudaFree(mailbox);
+  if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string("cudaFree(mailbox): ") + cudaGetErrorString(e));
+  return FSSIM_OK;
+}
+
+int fssim_ipc_get_handle(const void* mailbox, unsigned char handle[FSSIM_IPC_HANDLE_BYTES]) {
+  g_last_error.clear();
+  if (!mailbox || !handle) return fail(FSSIM_ERR_NULLPTR, "mailbox and handle are required");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(mailbox));
+  if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string("cudaIpcGetMemHandle: ") + cudaGetErrorString(e));
+  static_assert(sizeof(h) == FSSIM_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  return FSSIM_OK;
+}
+
+int fssim_ipc_open_handle(const unsigned char handle[FSSIM_IPC_HANDLE_BYTES], void** peer_mailbox) {
+  g_last_error.clear();
+  if (!handle || !peer_mailbox) return fail(FSSIM_ERR_NULLPTR, "handle and peer_mailbox are required");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+  *peer_mailbox = p;
+  return FSSIM_OK;
+}
+
+int fssim_ipc_close_handle(void* peer_mailbox) {
+  g_last_error.clear();
+  if (!peer_mailbox) return FSSIM_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(peer_mailbox);
+  if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string("cudaIpcCloseMemHandle: ") + cudaGetErrorString(e));
+  return FSSIM_OK;
+}
+
+int fssim_forward_dp(const fssim_forward_args* a, const fssim_dp_args* dp, fssim_stream_t stream) {
+  g_last_error.clear();
+  if (!a) return fail(FSSIM_ERR_NULLPTR, "args is NULL");
+  if (a->reduce != FSSIM_REDUCE_SCALAR) return fail(FSSIM_ERR_ARGUMENT, "fssim_forward_dp needs reduce = SCALAR");
+  fssim::DpParams p{};
+  int st = check_dp(dp, &p);
+  if (st) return st;
+  st = forward_impl(a, &p, stream);
+  if (st || a->B * a->C * a->H * a->W != 0) return st;
+  // an empty shard has no forward kernel to publish its (zero) sum
+  fssim::dp_publish_kernel<<<1, 32, 0, stream>>>(p, 0.0);
+  return launch_error("dp publish launch");
+}
+
+int fssim_dp_gather(const fssim_dp_args* dp, float scale, float* out, fssim_stream_t stream) {
+  g_last_error.clear();
+  if (!out) return fail(FSSIM_ERR_NULLPTR, "out is NULL");
+  fssim::DpParams p{};
+  const int st = check_dp(dp, &p);
+  if (st) return st;
+  fssim::dp_gather_kernel<<<1, 32, 0, stream>>>(p, scale, out);
+  return launch_error("dp gather launch");
 }
 
 int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {

@@ -550,8 +550,88 @@ __device__ __forceinline__ void vsumR(const float2 (&v)[kRPT + 2 * HALO], float2
 // ---------------------------------------------------------------------------------------
 // Forward kernel
 // ---------------------------------------------------------------------------------------
+// ---------------------------------------------------------------------------------------
+// Cross-GPU exchange of the per-rank SSIM sums (batch-sharded loss, one process per GPU)
+// ---------------------------------------------------------------------------------------
+// Every rank owns a mailbox in its own device memory, mapped into every other rank's
+// process (CUDA IPC), of 2 x world slots of {double sum; u64 seq}. At the end of the
+// forward, the last CTA stores the rank's sum into slot [seq & 1][rank] of every rank's
+// mailbox over NVLink (value, system fence, then seq). A one-warp gather kernel on each rank
+// waits, with a bounded poll, until all `world` slots of its own mailbox carry `seq`, then
+// sums them in rank order: the same bits on every rank. Two slot sets suffice: a rank
+// writes step seq+2 only after its gather of step seq+1, which needs every rank's step
+// seq+1 sum, which each rank publishes only after its own gather of step seq.
+constexpr int kMaxDpRanks = 8;
+constexpr unsigned kErrGatherTimeout = 2u;
+constexpr int kGatherPollLimit = 1 << 22;  // polls of 64 ns sleep: ~0.3 s before failing
+
+struct DpMailSlot {
+  double sum;
+  unsigned long long seq;
+};
+
+struct DpParams {
+  DpMailSlot* mail[kMaxDpRanks];  // mailbox of rank r as mapped in this process
+  int world;                      // 0: not sharded
+  int rank;
+  unsigned long long seq;
+};
+
+__device__ __forceinline__ void dp_publish(const DpParams& dp, double sum) {
+  const int set = static_cast<int>(dp.seq & 1ull);
+  for (int r = 0; r < dp.world; ++r) {
+    DpMailSlot* slot = dp.mail[r] + set * dp.world + dp.rank;
+    *reinterpret_cast<volatile double*>(&slot->sum) = sum;
+  }
+  __threadfence_system();
+  for (int r = 0; r < dp.world; ++r) {
+    DpMailSlot* slot = dp.mail[r] + set * dp.world + dp.rank;
+    *reinterpret_cast<volatile unsigned long long*>(&slot->seq) = dp.seq;
+  }
+}
+
+// Publishes a sum computed without the forward kernel (an empty shard publishes 0).
+__global__ void dp_publish_kernel(const DpParams dp, double sum) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) dp_publish(dp, sum);
+}
+
+// One warp: lane r < world waits for slot [seq & 1][r] of this rank's mailbox, then lane 0
+// writes out[0] = scale * (sum of the world sums in rank order).
+__global__ void __launch_bounds__(32) dp_gather_kernel(const DpParams dp, float scale, float* out) {
+  const int lane = threadIdx.x;
+  const int set = static_cast<int>(dp.seq & 1ull);
+  bool ok = true;
+  double v = 0.0;
+  if (lane < dp.world) {
+    const DpMailSlot* slot = dp.mail[dp.rank] + set * dp.world + lane;
+    const volatile unsigned long long* seqp =
+        reinterpret_cast<const volatile unsigned long long*>(&slot->seq);
+    int i = 0;
+    while (*seqp != dp.seq && i < kGatherPollLimit) {
+      __nanosleep(64);
+      ++i;
+    }
+    ok = (*seqp == dp.seq);
+    __threadfence_system();
+    v = *reinterpret_cast<const volatile double*>(&slot->sum);
+  }
+  const bool all_ok = __all_sync(0xffffffffu, ok);
+  if (!all_ok) {
+    if (lane == 0) {
+      atomicOr(&g_device_error, kErrGatherTimeout);
+      out[0] = __int_as_float(0x7fc00000);  // NaN
+    }
+    return;
+  }
+  // rank-ordered sum (lane 0 reads the others' values through shuffles)
+  double total = 0.0;
+  for (int r = 0; r < dp.world; ++r) total += __shfl_sync(0xffffffffu, v, r);
+  if (lane == 0) out[0] = static_cast<float>(total * static_cast<double>(scale));
+}
+
 struct FwdParams {
   CUtensorMap tmap[2];   // img1, img2 as (W, H, planes), boxes of 8 rows (when use_tma)
+  DpParams dp;           // sharded loss: publish the batch sum to every rank (dp.world > 0)
   const void* img1;
   const void* img2;
   float* map;            // optional per-pixel SSIM (unmasked)
@@ -891,7 +971,10 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   }
   if (a.reduce == 1) {
     const double total = block_sum(local, red);
-    if (threadIdx.x == 0) a.out[0] = static_cast<float>(total * static_cast<double>(a.out_scale));
+    if (threadIdx.x == 0) {
+      a.out[0] = static_cast<float>(total * static_cast<double>(a.out_scale));
+      if (a.dp.world > 0) dp_publish(a.dp, total);
+    }
   }
 }
 

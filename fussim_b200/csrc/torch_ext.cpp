@@ -199,9 +199,10 @@ torch::Tensor workspace_for(const torch::Tensor& like, int64_t B) {
 //   out        () for reduce == 1, (B,) for reduce == 2, FP32;
 //   partials   (3, B, C, H, W) in FP32 or FP16, or an empty tensor when !train;
 //   image_sums (B,) FP64 per-image sums of the (cropped, clamped) map.
-std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward(
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward_impl(
     torch::Tensor img1, torch::Tensor img2, int window_size, double C1, double C2, bool valid,
-    bool clamp, bool train, int reduce, bool half_partials, double out_scale) {
+    bool clamp, bool train, int reduce, bool half_partials, double out_scale,
+    const fssim_dp_args* dp) {
   check_window(window_size);
   check_cuda_4d(img1, "img1");
   check_cuda_4d(img2, "img2");
@@ -246,8 +247,77 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward(
   args.image_sums = sums.data_ptr<double>();
   args.workspace = ws.data_ptr();
   args.workspace_bytes = static_cast<size_t>(ws.numel()) * 8;
-  check_status(fssim_forward(&args, current_stream()));
+  check_status(dp ? fssim_forward_dp(&args, dp, current_stream())
+                  : fssim_forward(&args, current_stream()));
   return {out, partials, sums};
+}
+
+std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward(
+    torch::Tensor img1, torch::Tensor img2, int window_size, double C1, double C2, bool valid,
+    bool clamp, bool train, int reduce, bool half_partials, double out_scale) {
+  return loss_forward_impl(img1, img2, window_size, C1, C2, valid, clamp, train, reduce,
+                           half_partials, out_scale, nullptr);
+}
+
+// ---- batch-sharded loss: peer mailboxes over CUDA IPC ----
+fssim_dp_args make_dp(int64_t world, int64_t rank, int64_t seq,
+                      const std::vector<int64_t>& mailboxes) {
+  TORCH_CHECK(world >= 1 && world <= FSSIM_DP_MAX_RANKS, "world out of range");
+  TORCH_CHECK(static_cast<int64_t>(mailboxes.size()) == world, "one mailbox per rank");
+  fssim_dp_args d{};
+  d.world = static_cast<int32_t>(world);
+  d.rank = static_cast<int32_t>(rank);
+  d.seq = static_cast<uint64_t>(seq);
+  for (int64_t r = 0; r < world; ++r) d.mailboxes[r] = reinterpret_cast<void*>(mailboxes[r]);
+  return d;
+}
+
+// Forward of this rank's shard (reduce = scalar) that also publishes its sum to every rank.
+std::tuple<torch::Tensor, torch::Tensor> loss_forward_dp(
+    torch::Tensor img1, torch::Tensor img2, int window_size, double C1, double C2, bool valid,
+    bool train, double out_scale, int64_t world, int64_t rank, int64_t seq,
+    std::vector<int64_t> mailboxes) {
+  const fssim_dp_args d = make_dp(world, rank, seq, mailboxes);
+  auto r = loss_forward_impl(img1, img2, window_size, C1, C2, valid, false, train, 1, false,
+                             out_scale, &d);
+  return {std::get<0>(r), std::get<1>(r)};
+}
+
+// out (a 0-d FP32 CUDA tensor) = scale * the sum over ranks of step seq.
+void dp_gather(torch::Tensor out, double scale, int64_t world, int64_t rank, int64_t seq,
+               std::vector<int64_t> mailboxes) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.numel() == 1,
+              "out must be a one-element float32 CUDA tensor");
+  const at::cuda::OptionalCUDAGuard guard(out.device());
+  const fssim_dp_args d = make_dp(world, rank, seq, mailboxes);
+  check_status(fssim_dp_gather(&d, static_cast<float>(scale), out.data_ptr<float>(),
+                               current_stream()));
+}
+
+int64_t dp_mailbox_alloc(int64_t world) {
+  void* p = nullptr;
+  check_status(fssim_dp_mailbox_alloc(static_cast<int>(world), &p));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void dp_mailbox_free(int64_t ptr) { check_status(fssim_dp_mailbox_free(reinterpret_cast<void*>(ptr))); }
+
+py::bytes ipc_get_handle(int64_t ptr) {
+  unsigned char h[FSSIM_IPC_HANDLE_BYTES];
+  check_status(fssim_ipc_get_handle(reinterpret_cast<void*>(ptr), h));
+  return py::bytes(reinterpret_cast<const char*>(h), FSSIM_IPC_HANDLE_BYTES);
+}
+
+int64_t ipc_open_handle(py::bytes handle) {
+  const std::string h = handle;
+  TORCH_CHECK(h.size() == FSSIM_IPC_HANDLE_BYTES, "IPC handle must be 64 bytes");
+  void* p = nullptr;
+  check_status(fssim_ipc_open_handle(reinterpret_cast<const unsigned char*>(h.data()), &p));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close_handle(int64_t ptr) {
+  check_status(fssim_ipc_close_handle(reinterpret_cast<void*>(ptr)));
 }
 
 torch::Tensor loss_backward(torch::Tensor grad_out, torch::Tensor img1, torch::Tensor img2,
@@ -300,5 +370,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fusedssim_fp16_backward", &fusedssim_fp16_backward);
   m.def("loss_forward", &loss_forward);
   m.def("loss_backward", &loss_backward);
+  m.def("loss_forward_dp", &loss_forward_dp);
+  m.def("dp_gather", &dp_gather);
+  m.def("dp_mailbox_alloc", &dp_mailbox_alloc);
+  m.def("dp_mailbox_free", &dp_mailbox_free);
+  m.def("ipc_get_handle", &ipc_get_handle);
+  m.def("ipc_open_handle", &ipc_open_handle);
+  m.def("ipc_close_handle", &ipc_close_handle);
   m.def("version", &version);
+  m.def("set_reserved_sms", [](int n) {
+    const int st = fssim_set_reserved_sms(n);
+    if (st != FSSIM_OK) throw std::invalid_argument(fssim_last_error());
+  });
 }

@@ -66,6 +66,12 @@ const char* fssim_version(void);
  * workspace not zero-filled). Synchronises with the device. clear != 0 resets the flag. */
 int fssim_poll_device_error(unsigned* code, int clear);
 
+/* Number of SMs the kernels' persistent grids leave unused (default 0), for callers that
+ * run another kernel concurrently, e.g. a collective overlapping the backward: a grid that
+ * fills every SM would otherwise wait for that kernel's blocks to leave before its last
+ * CTAs start. Process-wide; n >= 0 (FSSIM_ERR_ARGUMENT otherwise). */
+int fssim_set_reserved_sms(int n);
+
 /* ------------------------------------------------------------------------------------
  * 1. Reference extension functions (map-producing compat seam)
  * ------------------------------------------------------------------------------------ */
@@ -190,6 +196,54 @@ int fssim_backward(const fssim_backward_args* args, fssim_stream_t stream);
  * on each device performs a one-time set-up (cudaGetSymbolAddress) and should come before
  * any stream capture on that device. */
 int fssim_forward_noalloc(const fssim_forward_args* args, fssim_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * 3. Batch-sharded loss over several GPUs (one process per GPU, no counterpart in the
+ *    reference). The global mean over all ranks' shards is formed without a collective
+ *    library call: the forward's last CTA stores the rank's sum into every rank's mailbox
+ *    over NVLink (CUDA IPC mappings), and a one-warp gather kernel on each rank sums the
+ *    world values in rank order (identical bits on every rank).
+ *
+ *    Set-up, once per group: each rank allocates its mailbox (fssim_dp_mailbox_alloc),
+ *    exports it (fssim_ipc_get_handle), exchanges the handles with the other ranks by any
+ *    host channel, and maps the peers' mailboxes (fssim_ipc_open_handle).
+ *    Per step: every rank calls fssim_forward_dp with the same seq (1, 2, 3, ...), then
+ *    fssim_dp_gather. The gather waits for the other ranks with a bounded poll (about
+ *    0.3 s); on time-out it writes NaN and sets bit 1 of fssim_poll_device_error.
+ * ------------------------------------------------------------------------------------ */
+
+#define FSSIM_DP_MAX_RANKS 8
+#define FSSIM_IPC_HANDLE_BYTES 64
+
+typedef struct fssim_dp_args {
+  int32_t world;                          /* ranks (1..FSSIM_DP_MAX_RANKS) */
+  int32_t rank;                           /* this rank */
+  uint64_t seq;                           /* step number, >= 1, the same on every rank */
+  void* mailboxes[FSSIM_DP_MAX_RANKS];    /* mailbox of rank r as mapped in this process */
+} fssim_dp_args;
+
+/* Bytes of one mailbox for `world` ranks. */
+size_t fssim_dp_mailbox_bytes(int world);
+
+/* Allocates (cudaMalloc, a whole allocation) and zero-fills this rank's mailbox on the
+ * current device; fssim_dp_mailbox_free releases it. */
+int fssim_dp_mailbox_alloc(int world, void** mailbox);
+int fssim_dp_mailbox_free(void* mailbox);
+
+/* CUDA IPC export of a mailbox, and mapping / unmapping of a peer's exported mailbox. */
+int fssim_ipc_get_handle(const void* mailbox, unsigned char handle[FSSIM_IPC_HANDLE_BYTES]);
+int fssim_ipc_open_handle(const unsigned char handle[FSSIM_IPC_HANDLE_BYTES],
+                          void** peer_mailbox);
+int fssim_ipc_close_handle(void* peer_mailbox);
+
+/* fssim_forward of this rank's shard (reduce must be FSSIM_REDUCE_SCALAR), which also
+ * publishes the shard's FP64 sum to every rank's mailbox. out[0] receives the local
+ * out_scale * sum; fssim_dp_gather replaces it with the global value. */
+int fssim_forward_dp(const fssim_forward_args* args, const fssim_dp_args* dp,
+                     fssim_stream_t stream);
+
+/* out[0] = scale * (sum of the world ranks' published sums of step dp->seq, rank order). */
+int fssim_dp_gather(const fssim_dp_args* dp, float scale, float* out, fssim_stream_t stream);
 
 #ifdef __cplusplus
 }

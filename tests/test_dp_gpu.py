@@ -1,0 +1,96 @@
+"""The batch-sharded path on 2 GPUs (NCCL), against the single-GPU fused loss.
+
+Runs only where two GPUs are visible. Two child processes (one per GPU) each hold one shard
+of a seeded global batch; the value of fused_ssim_dp must equal fused_ssim of the whole
+batch on one GPU, and each rank's gradient the matching slice of its gradient. NVLink
+SHARP reductions are switched off (NCCL_NVLS_ENABLE=0). The shard sums travel through the
+peer mailboxes (CUDA IPC over NVLink); NCCL carries only the one-time set-up (the pixel
+count and the exchange of the IPC handles).
+"""
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+SHARDS = (1, 2)
+SHAPE = (3, 96, 200)
+
+
+def _free_port():
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _global_pair():
+    from fussim_b200 import synthetic
+
+    return synthetic.pair_noise((sum(SHARDS),) + SHAPE, 0.1, seed=31)
+
+
+def _worker(rank, port, queue):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=2, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from fussim_b200 import distributed as D
+
+        a_all, b_all = _global_pair()
+        lo = sum(SHARDS[:rank])
+        out = {}
+        for padding in ("same", "valid"):
+            a = a_all[lo:lo + SHARDS[rank]].to(dev).requires_grad_(True)
+            b = b_all[lo:lo + SHARDS[rank]].to(dev)
+            v, work = D.fused_ssim_dp(a, b, padding=padding, async_op=True)
+            v.backward()
+            work.wait()
+            torch.cuda.synchronize()
+            out[padding] = (float(v.detach()), a.grad.cpu().numpy().copy())
+        # the peer path (mailboxes over CUDA IPC) must have been used, not a collective
+        out["peer"] = len(D._mailboxes) == 1
+        D.release_mailboxes()
+        queue.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_dp_two_gpus_matches_single_gpu():
+    import fussim_b200 as fb
+
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = mp.start_processes(_worker, args=(_free_port(), queue), nprocs=2, join=False,
+                               start_method="spawn")
+    res = {}
+    for _ in range(2):
+        rank, r = queue.get(timeout=180)
+        res[rank] = r
+    while not procs.join(timeout=120):
+        pass
+    a_all, b_all = _global_pair()
+    assert res[0]["peer"] and res[1]["peer"]
+    for padding in ("same", "valid"):
+        x = a_all.cuda().requires_grad_(True)
+        v = fb.fused_ssim(x, b_all.cuda(), padding=padding)
+        v.backward()
+        g = x.grad.cpu()
+        for rank in range(2):
+            val, grad = res[rank][padding]
+            assert abs(val - v.item()) <= 1e-6
+            lo = sum(SHARDS[:rank])
+            ref = g[lo:lo + SHARDS[rank]]
+            assert (torch.from_numpy(grad) - ref).abs().max().item() <= 1e-5 * ref.abs().max().item()
