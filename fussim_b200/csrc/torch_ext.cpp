@@ -360,6 +360,54 @@ torch::Tensor loss_backward(torch::Tensor grad_out, torch::Tensor img1, torch::T
 
 std::string version() { return fssim_version(); }
 
+// The fused loss as a C++ autograd function: the same forward and backward as the Python
+// _FusedSSIMLoss, without the Python layer in either direction (the backward runs on the
+// autograd engine thread without taking the GIL). Inputs are converted for the kernels
+// inside the forward (not recorded), and the gradient is returned in img1's dtype.
+struct FusedLossFn : public torch::autograd::Function<FusedLossFn> {
+  static torch::Tensor forward(torch::autograd::AutogradContext* ctx, torch::Tensor img1,
+                               torch::Tensor img2, double C1, double C2, int64_t window_size,
+                               bool valid, bool clamp, int64_t reduce, bool half,
+                               double scale, double chain_scale) {
+    torch::Tensor a, b;
+    if (half) {
+      a = img1.scalar_type() == at::kHalf ? img1 : img1.to(at::kHalf);
+      b = img2.scalar_type() == at::kHalf ? img2 : img2.to(at::kHalf);
+    } else {
+      a = img1;
+      b = img2.scalar_type() == img1.scalar_type() ? img2 : img2.to(img1.scalar_type());
+    }
+    auto r = loss_forward_impl(a, b, static_cast<int>(window_size), C1, C2, valid, clamp, true,
+                               static_cast<int>(reduce), false, scale, nullptr);
+    ctx->save_for_backward({a, b, std::get<1>(r)});
+    ctx->saved_data["ws"] = window_size;
+    ctx->saved_data["per_image"] = reduce == 2;
+    ctx->saved_data["chain"] = chain_scale;
+    ctx->saved_data["gdt"] = static_cast<int64_t>(dtype_code(img1.scalar_type()));
+    return std::get<0>(r);
+  }
+
+  static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
+                                                 torch::autograd::variable_list grads) {
+    const auto saved = ctx->get_saved_variables();
+    auto grad = loss_backward(grads[0], saved[0], saved[1], saved[2],
+                              static_cast<int>(ctx->saved_data["ws"].toInt()),
+                              ctx->saved_data["per_image"].toBool(),
+                              ctx->saved_data["chain"].toDouble(),
+                              static_cast<int>(ctx->saved_data["gdt"].toInt()));
+    return {grad,            torch::Tensor(), torch::Tensor(), torch::Tensor(),
+            torch::Tensor(), torch::Tensor(), torch::Tensor(), torch::Tensor(),
+            torch::Tensor(), torch::Tensor(), torch::Tensor()};
+  }
+};
+
+torch::Tensor fused_loss(torch::Tensor img1, torch::Tensor img2, double C1, double C2,
+                         int64_t window_size, bool valid, bool clamp, int64_t reduce, bool half,
+                         double scale, double chain_scale) {
+  return FusedLossFn::apply(img1, img2, C1, C2, window_size, valid, clamp, reduce, half, scale,
+                            chain_scale);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -370,6 +418,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fusedssim_fp16_backward", &fusedssim_fp16_backward);
   m.def("loss_forward", &loss_forward);
   m.def("loss_backward", &loss_backward);
+  m.def("fused_loss", &fused_loss);
   m.def("loss_forward_dp", &loss_forward_dp);
   m.def("dp_gather", &dp_gather);
   m.def("dp_mailbox_alloc", &dp_mailbox_alloc);

@@ -181,39 +181,17 @@ def _kernel_inputs(img1, img2, half):
     return img1, (img2 if img2.dtype == img1.dtype else img2.to(img1.dtype))
 
 
-class _FusedSSIMLoss(torch.autograd.Function):
-    """mean / per-image mean of the (cropped, clamped) SSIM map, gradient to img1."""
-
-    @staticmethod
-    def forward(ctx, img1, img2, C1, C2, window_size, valid, clamp, reduce, half):
-        ext = _ensure_cuda_extension()
-        grad_dtype = _DTYPE_CODE.get(img1.dtype, 0)
-        a, b = _kernel_inputs(img1, img2, half)
-        scale = _inv(_count(a.shape, window_size, valid, reduce == _REDUCE_PER_IMAGE))
-        out, partials, _ = ext.loss_forward(a, b, window_size, C1, C2, valid, clamp, True,
-                                            reduce, False, scale)
-        ctx.save_for_backward(a, b, partials)
-        ctx.window_size = window_size
-        ctx.per_image = reduce == _REDUCE_PER_IMAGE
-        # d(out)/d(map) = 1/count; with nothing counted (an empty valid crop) no pixel
-        # receives gradient, as the reference's zero-filled dL/dmap gives.
-        ctx.scale = scale if scale != float("inf") else 0.0
-        ctx.grad_dtype = grad_dtype
-        return out
-
-    @staticmethod
-    def backward(ctx, grad_out):
-        ext = _ensure_cuda_extension()
-        a, b, partials = ctx.saved_tensors
-        grad = ext.loss_backward(grad_out, a, b, partials, ctx.window_size, ctx.per_image,
-                                 ctx.scale, ctx.grad_dtype)
-        return grad, None, None, None, None, None, None, None, None
-
-
 def _reduce(img1, img2, C1, C2, window_size, valid, clamp, reduce, train, half):
-    if train:
-        return _FusedSSIMLoss.apply(img1, img2, C1, C2, window_size, valid, clamp, reduce, half)
     ext = _ensure_cuda_extension()
+    if train:
+        # autograd function implemented in the extension (C++): forward = fused kernel with
+        # partials and in-kernel mean, backward = one kernel; d(out)/d(map) = 1/count, and
+        # with nothing counted (an empty valid crop) no pixel receives gradient, as the
+        # reference's zero-filled dL/dmap gives
+        scale = _inv(_count(img1.shape, window_size, valid, reduce == _REDUCE_PER_IMAGE))
+        chain = scale if scale != float("inf") else 0.0
+        return ext.fused_loss(img1, img2, C1, C2, window_size, valid, clamp, reduce, half,
+                              scale, chain)
     a, b = _kernel_inputs(img1, img2, half)
     scale = _inv(_count(a.shape, window_size, valid, reduce == _REDUCE_PER_IMAGE))
     out, _, _ = ext.loss_forward(a, b, window_size, C1, C2, valid, clamp, False, reduce, False,
