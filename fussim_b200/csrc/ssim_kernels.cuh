@@ -484,23 +484,24 @@ __device__ __forceinline__ unsigned tma_step_bytes(int nh) {
   return static_cast<unsigned>(NMAP * nbox * kBoxRows * StagePitch<T>::value * sizeof(T));
 }
 
-// TMA staging of one step, issued by a single thread: rows [h0, h0+nh) rounded up to whole
-// boxes, columns [x0-8, x0-8+pitch) of plane s.plane for each of the NMAP tensor maps, into
-// rows [slot, slot + nh) of the layout [NMAP][SROWS][pitch]. Rows or columns outside the
-// image arrive as zeros.
+// TMA staging of one step by the lanes of one warp, one box per lane: rows [h0, h0+nh)
+// rounded up to whole boxes, columns [x0-8, x0-8+pitch) of plane s.plane for each of the
+// NMAP tensor maps, into rows [slot, slot + nh) of the layout [NMAP][SROWS][pitch]; rows or
+// columns outside the image arrive as zeros. Lane lane0 + m*nbox + b issues box b of map m. Every issuing lane first orders the CTA's
+// earlier shared-memory reads of the slot (made visible by a CTA barrier) before its copy.
 template <typename T, int NMAP, int SROWS, typename StepT>
-__device__ __forceinline__ void stage_tma(T* sm, const CUtensorMap* maps, const StepT& s,
-                                          uint64_t* bar) {
+__device__ __forceinline__ void stage_tma_lanes(T* sm, const CUtensorMap* maps, const StepT& s,
+                                                uint64_t* bar, int lane0) {
   constexpr int P = StagePitch<T>::value;
   const int nbox = (s.nh() + kBoxRows - 1) / kBoxRows;
-  const int x0 = s.strip * kStrip - kLeft;
-  const int z = s.plane;
-  const int h0 = s.h0();
-#pragma unroll
-  for (int m = 0; m < NMAP; ++m)
-    for (int b = 0; b < nbox; ++b)
-      tma_load_3d(sm + (m * SROWS + s.slot + b * kBoxRows) * P, maps + m, x0,
-                  h0 + b * kBoxRows, z, bar);
+  const int l = static_cast<int>(threadIdx.x & 31) - lane0;
+  if (l >= 0 && l < NMAP * nbox) {
+    const int m = l / nbox;
+    const int b = l - m * nbox;
+    fence_proxy_async_smem();
+    tma_load_3d(sm + (m * SROWS + s.slot + b * kBoxRows) * P, maps + m,
+                s.strip * kStrip - kLeft, s.h0() + b * kBoxRows, s.plane, bar);
+  }
 }
 
 // Copy ring rows [kRows, kRows + 2*HALO) to [0, 2*HALO): the vertical halo for the next
@@ -769,12 +770,18 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   }
   __syncthreads();
   Step<HALO> cur = first_step<HALO>(beg, end, g);
+  // TMA staging of a step by warp 0: lane 0 posts the byte count, the lanes issue the boxes
+  auto issue = [&](const Step<HALO>& st) {
+    if (warp == 0) {
+      if (lane == 0) mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(st.nh()));
+      stage_tma_lanes<TIn, 2, SROWS>(stg, a.tmap, st, &bar, 0);
+    }
+  };
   if (cur.n) {
     if (!tma) {
       stage<TIn, 2, SROWS>(stg, src, g, cur, a.aligned16);
-    } else if (threadIdx.x == 0) {
-      mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(cur.nh()));
-      stage_tma<TIn, 2, SROWS>(stg, a.tmap, cur, &bar);
+    } else {
+      issue(cur);
     }
   }
   unsigned phase = 0;
@@ -801,21 +808,15 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
     Step<HALO> nxt = next_step<HALO>(cur, g);
     const bool early = tma && nxt.n && !cur.first && !nxt.first;
     nxt.slot = early ? (cur.slot ^ kRows) : 0;
-    if (early && threadIdx.x == 0) {
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(nxt.nh()));
-      stage_tma<TIn, 2, SROWS>(stg, a.tmap, nxt, &bar);
-    }
+    if (early) issue(nxt);
     fwd_hpass<HALO, TIn, SROWS, MERGED>(stg + cur.slot * SP, stg + (SROWS + cur.slot) * SP, ring,
                                         cur.nh(), cur.hdst(), T);
     __syncthreads();
     if (nxt.n && !early) {
       if (!tma) {
         stage<TIn, 2, SROWS>(stg, src, g, nxt, a.aligned16);
-      } else if (threadIdx.x == 0) {
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&bar, tma_step_bytes<TIn, 2>(nxt.nh()));
-        stage_tma<TIn, 2, SROWS>(stg, a.tmap, nxt, &bar);
+      } else {
+        issue(nxt);
       }
     }
 
@@ -1099,15 +1100,25 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
   }
   __syncthreads();
   Step<HALO> cur = first_step<HALO>(beg, end, g);
+  // TMA staging of a step by warp 0: lane 0 posts the byte count, the lanes issue the boxes
+  auto issue = [&](const Step<HALO>& st) {
+    if (warp == 0) {
+      if (lane == 0)
+        mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(st.nh()) +
+                                        (DLMAP ? tma_step_bytes<float, 1>(st.nh()) : 0u));
+      stage_tma_lanes<TP, 3, SROWS>(stg, a.tmap, st, &bar, 0);
+      if (DLMAP) {
+        const int nbox = (st.nh() + kBoxRows - 1) / kBoxRows;
+        stage_tma_lanes<float, 1, SROWS>(sdl, a.tmap + 3, st, &bar, 3 * nbox);
+      }
+    }
+  };
   if (cur.n) {
     if (!tma) {
       stage<TP, 3, SROWS>(stg, src, g, cur, a.aligned16);
       if (DLMAP) stage<float, 1, SROWS>(sdl, dsrc, g, cur, a.aligned16);
-    } else if (threadIdx.x == 0) {
-      mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(cur.nh()) +
-                                      (DLMAP ? tma_step_bytes<float, 1>(cur.nh()) : 0u));
-      stage_tma<TP, 3, SROWS>(stg, a.tmap, cur, &bar);
-      if (DLMAP) stage_tma<float, 1, SROWS>(sdl, a.tmap + 3, cur, &bar);
+    } else {
+      issue(cur);
     }
   }
   unsigned phase = 0;
@@ -1163,13 +1174,7 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
     Step<HALO> nxt = next_step<HALO>(cur, g);
     const bool early = tma && nxt.n && !cur.first && !nxt.first;
     nxt.slot = early ? (cur.slot ^ kRows) : 0;
-    if (early && threadIdx.x == 0) {
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(nxt.nh()) +
-                                      (DLMAP ? tma_step_bytes<float, 1>(nxt.nh()) : 0u));
-      stage_tma<TP, 3, SROWS>(stg, a.tmap, nxt, &bar);
-      if (DLMAP) stage_tma<float, 1, SROWS>(sdl, a.tmap + 3, nxt, &bar);
-    }
+    if (early) issue(nxt);
     bwd_hpass<HALO, TIn, TP, DLMAP, SROWS>(stg + cur.slot * Cfg::kSP,
                                            sdl + cur.slot * StagePitch<float>::value, ring,
                                            cur.nh(), cur.hdst(), T);
@@ -1178,12 +1183,8 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
       if (!tma) {
         stage<TP, 3, SROWS>(stg, src, g, nxt, a.aligned16);
         if (DLMAP) stage<float, 1, SROWS>(sdl, dsrc, g, nxt, a.aligned16);
-      } else if (threadIdx.x == 0) {
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(nxt.nh()) +
-                                        (DLMAP ? tma_step_bytes<float, 1>(nxt.nh()) : 0u));
-        stage_tma<TP, 3, SROWS>(stg, a.tmap, nxt, &bar);
-        if (DLMAP) stage_tma<float, 1, SROWS>(sdl, a.tmap + 3, nxt, &bar);
+      } else {
+        issue(nxt);
       }
     }
 
