@@ -70,12 +70,12 @@ constexpr int kLG = 32 / kRG;                 // lane groups per warp (1 or 2)
 constexpr int kJJ = 2 / kLG;                  // chunk iterations per thread per group
 static_assert(kRows == 16 || kRows == 32, "steps of 16 or 32 rows");
 
-// Staged rows per map: MaxRows rounded up to whole TMA boxes of 8 rows, and at least two
+// Staged rows per map: MaxRows rounded up to whole TMA boxes of 16 rows, and at least two
 // slots of kRows rows, so a step can be staged into one slot while the H-pass reads the
 // other. The map stride (rows x pitch x element size) is then a multiple of 128 bytes, as
 // is every box start.
 template <int HALO> struct StageRows {
-  static constexpr int kBoxed = (MaxRows<HALO>::value + 7) / 8 * 8;
+  static constexpr int kBoxed = (MaxRows<HALO>::value + 15) / 16 * 16;
   static constexpr int value = kBoxed > 2 * kRows ? kBoxed : 2 * kRows;
 };
 
@@ -162,11 +162,11 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // Staging with the tensor memory accelerator (TMA)
 // ---------------------------------------------------------------------------------------
 // When every staged plane is 16-byte aligned with a row pitch that is a multiple of 16
-// bytes, one thread stages a step with a handful of tiled bulk copies (boxes of kBoxRows
+// bytes, warp 0 stages a step with a handful of tiled bulk copies (boxes of kBoxRows
 // rows x one staged row pitch of columns, zero-filled outside the image by the copy unit)
 // that complete on an mbarrier. This replaces 2-4 cp.async chunks per thread per staged
 // row and all their address arithmetic. Each copy reads this GPU's own memory into this CTA only.
-constexpr int kBoxRows = 8;
+constexpr int kBoxRows = 16;  // one box per map for a regular step
 constexpr int kWaitLimit = 1 << 20;  // bounded mbarrier polls before a step reports failure
 
 // Device-side failure codes (OR-ed into g_device_error, read by fssim_poll_device_error).
@@ -660,6 +660,9 @@ struct FwdConfig {
   static constexpr int kMaps = MERGED ? 4 : 5;
   static constexpr int kMaxR = MaxRows<HALO>::value;
   static constexpr int kSRows = StageRows<HALO>::value;
+  // a first step's boxes fit the staging rows; a regular step's boxes fit one slot
+  static_assert(kSRows >= (kMaxR + kBoxRows - 1) / kBoxRows * kBoxRows, "staging rows");
+  static_assert(kRows % kBoxRows == 0 && kSRows >= 2 * kRows, "staging slots");
   static constexpr int kSP = StagePitch<TIn>::value;
   static constexpr int kRP = RingPitch<kMaps>::value;
   static constexpr size_t kStageBytes = 2ull * kSRows * kSP * sizeof(TIn);
@@ -1002,6 +1005,9 @@ struct BwdConfig {
   static constexpr bool kHalfW = sizeof(TIn) == 2;
   static constexpr int kMaxR = MaxRows<HALO>::value;
   static constexpr int kSRows = StageRows<HALO>::value;
+  // a first step's boxes fit the staging rows; a regular step's boxes fit one slot
+  static_assert(kSRows >= (kMaxR + kBoxRows - 1) / kBoxRows * kBoxRows, "staging rows");
+  static_assert(kRows % kBoxRows == 0 && kSRows >= 2 * kRows, "staging slots");
   static constexpr int kSP = StagePitch<TP>::value;
   static constexpr int kRP = RingPitch<3>::value;
   static constexpr size_t kStageBytes = 3ull * kSRows * kSP * sizeof(TP);
