@@ -195,7 +195,7 @@ int launch_fwd(const fssim::FwdParams& p, cudaStream_t stream) {
   st = device_sms(&sms);
   if (st) return st;
   const int grid = grid_size(p.g, occ, sms);
-  if ((p.g.LT + grid - 1) / grid > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
+  if ((p.g.LT + grid - 1) / grid + 2 * p.g.H > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
   k<<<grid, fssim::kThreads, Cfg::kSmem, stream>>>(p);
   return launch_error("ssim forward launch");
 }
@@ -212,7 +212,7 @@ int launch_bwd(const fssim::BwdParams& p, cudaStream_t stream) {
   st = device_sms(&sms);
   if (st) return st;
   const int grid = grid_size(p.g, occ, sms);
-  if ((p.g.LT + grid - 1) / grid > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
+  if ((p.g.LT + grid - 1) / grid + 2 * p.g.H > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
   k<<<grid, fssim::kThreads, Cfg::kSmem, stream>>>(p);
   return launch_error("ssim backward launch");
 }

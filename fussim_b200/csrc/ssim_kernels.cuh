@@ -356,6 +356,23 @@ struct Step {
   __device__ __forceinline__ bool last() const { return t + n == t_end; }  // last step of the part
 };
 
+// Start of CTA b's range of strip-rows (b = 0..G; b = G gives LT). The split is even in
+// "work" rather than in rows: a column run part costs its rows plus about HALO rows for
+// the halo rows its first step computes, so each run is counted as H + HALO units and a
+// CTA boundary that would fall in a run's extra units moves to the next run's start.
+// Boundaries inside a run are rounded down to whole steps, so only a run's last step is
+// partial. Adjacent CTAs compute the shared boundary identically.
+template <int HALO>
+__device__ __forceinline__ int64_t cta_range_start(const Geometry& g, int64_t b, int64_t G) {
+  const int64_t runs = g.LT / g.H;
+  const int64_t per = g.H + HALO;
+  const int64_t A = (runs * per * b) / G;
+  const int64_t r = A / per;
+  const int64_t o = A - r * per;
+  if (o >= g.H) return (r + 1) * g.H;
+  return r * g.H + (o / kRows) * kRows;
+}
+
 template <int HALO>
 __device__ __forceinline__ Step<HALO> first_step(int64_t beg, int64_t end, const Geometry& g) {
   Step<HALO> s;
@@ -757,8 +774,8 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   __shared__ uint64_t bar;
 
   const Geometry& g = a.g;
-  const int64_t beg = (g.LT * blockIdx.x) / gridDim.x;
-  const int64_t end = (g.LT * (blockIdx.x + 1)) / gridDim.x;
+  const int64_t beg = cta_range_start<HALO>(g, blockIdx.x, gridDim.x);
+  const int64_t end = cta_range_start<HALO>(g, blockIdx.x + 1, gridDim.x);
   const TIn* const src[2] = {static_cast<const TIn*>(a.img1), static_cast<const TIn*>(a.img2)};
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r0 = warp * kRPT;
@@ -1086,8 +1103,8 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
   __shared__ uint64_t bar;
 
   const Geometry& g = a.g;
-  const int64_t beg = (g.LT * blockIdx.x) / gridDim.x;
-  const int64_t end = (g.LT * (blockIdx.x + 1)) / gridDim.x;
+  const int64_t beg = cta_range_start<HALO>(g, blockIdx.x, gridDim.x);
+  const int64_t end = cta_range_start<HALO>(g, blockIdx.x + 1, gridDim.x);
   const TP* const src[3] = {static_cast<const TP*>(a.p0), static_cast<const TP*>(a.p1),
                             static_cast<const TP*>(a.p2)};
   const float* const dsrc[1] = {a.dl};
