@@ -177,6 +177,24 @@ void set_bwd_tma(fssim::BwdParams& p, size_t pesize) {
   p.use_tma = ok;
 }
 
+// Launch with programmatic stream serialization allowed: the kernel may begin while the
+// previous kernel on the stream finishes; it waits (griddepcontrol.wait) before touching
+// global memory.
+template <typename Kernel, typename Params>
+cudaError_t launch_pdl(Kernel k, int grid, size_t smem, cudaStream_t stream, const Params& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(fssim::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, p);
+}
+
 int launch_error(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
@@ -196,7 +214,11 @@ int launch_fwd(const fssim::FwdParams& p, cudaStream_t stream) {
   if (st) return st;
   const int grid = grid_size(p.g, occ, sms);
   if ((p.g.LT + grid - 1) / grid + 2 * p.g.H > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
-  k<<<grid, fssim::kThreads, Cfg::kSmem, stream>>>(p);
+  const cudaError_t e = launch_pdl(k, grid, Cfg::kSmem, stream, p);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return fail(FSSIM_ERR_CUDA, std::string("ssim forward launch: ") + cudaGetErrorString(e));
+  }
   return launch_error("ssim forward launch");
 }
 
@@ -213,7 +235,11 @@ int launch_bwd(const fssim::BwdParams& p, cudaStream_t stream) {
   if (st) return st;
   const int grid = grid_size(p.g, occ, sms);
   if ((p.g.LT + grid - 1) / grid + 2 * p.g.H > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
-  k<<<grid, fssim::kThreads, Cfg::kSmem, stream>>>(p);
+  const cudaError_t e = launch_pdl(k, grid, Cfg::kSmem, stream, p);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return fail(FSSIM_ERR_CUDA, std::string("ssim backward launch: ") + cudaGetErrorString(e));
+  }
   return launch_error("ssim backward launch");
 }
 

@@ -216,6 +216,18 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// Programmatic dependent launch. The kernels are launched so that they may start while the
+// previous kernel on the stream is finishing; their set-up (barrier init, step cursor)
+// overlaps that tail, and griddepcontrol.wait, before the first access to global memory,
+// waits for the previous kernel to complete and its writes to be visible. (Both are no-ops
+// for a regular launch.) A kernel then allows its own dependent to launch.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 
@@ -790,6 +802,8 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   }
   __syncthreads();
   Step<HALO> cur = first_step<HALO>(beg, end, g);
+  grid_dependency_wait();
+  grid_launch_dependents();
   // TMA staging of a step by warp 0: lane 0 posts the byte count, the lanes issue the boxes
   auto issue = [&](const Step<HALO>& st) {
     if (warp == 0) {
@@ -1123,6 +1137,8 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
   }
   __syncthreads();
   Step<HALO> cur = first_step<HALO>(beg, end, g);
+  grid_dependency_wait();
+  grid_launch_dependents();
   // TMA staging of a step by warp 0: lane 0 posts the byte count, the lanes issue the boxes
   auto issue = [&](const Step<HALO>& st) {
     if (warp == 0) {
