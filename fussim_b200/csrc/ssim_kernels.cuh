@@ -206,6 +206,10 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
+// Brings a tensor map into the descriptor cache ahead of its first copy.
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
 // One 3-D tiled bulk copy global -> shared (coordinates: column, row, plane).
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y,
                                             int z, uint64_t* bar) {
@@ -802,6 +806,7 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   }
   __syncthreads();
   Step<HALO> cur = first_step<HALO>(beg, end, g);
+  if (tma && threadIdx.x < 2) prefetch_tensormap(a.tmap + threadIdx.x);
   grid_dependency_wait();
   grid_launch_dependents();
   // TMA staging of a step by warp 0: lane 0 posts the byte count, the lanes issue the boxes
@@ -1137,6 +1142,7 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
   }
   __syncthreads();
   Step<HALO> cur = first_step<HALO>(beg, end, g);
+  if (tma && threadIdx.x < (DLMAP ? 4 : 3)) prefetch_tensormap(a.tmap + threadIdx.x);
   grid_dependency_wait();
   grid_launch_dependents();
   // TMA staging of a step by warp 0: lane 0 posts the byte count, the lanes issue the boxes
