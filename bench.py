@@ -54,7 +54,7 @@ BWD_FLOPS = 2 * 3 * 2 * 11 + 6        # 3 partial maps x 2 passes x 11 MACs, com
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each kernel on
 # this workload, from one ncu capture (profiles/ssim_fwd_bwd_1080p_fp32.md; the capture
 # flushes L2 before each launch, so it is the cold-L2 figure).
-NCU_TRAFFIC_BYTES = {"fwd": 61.06e6 + 28.30e6, "bwd": 175.63e6 + 15.76e6}
+NCU_TRAFFIC_BYTES = {"fwd": 60.70e6 + 27.22e6, "bwd": 172.88e6 + 15.12e6}
 
 
 def load_peaks():
@@ -391,6 +391,32 @@ def measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, step_ms
     out["fp16"] = {"workload": "8x3x1024x1024 fp16 inputs, autocast, padding valid, train, "
                                "fwd+bwd", "value": v16, "unit": "Mpix/s", "ms_per_step": t16,
                    "ratio_vs_fp32_1080p": v16 / v32, "steps": i16}
+    torch.cuda.synchronize()
+    del p16
+    # The data-parallel batch config (64x3x2048^2 FP32, U[0,1] + N(0, 0.1^2)) whole on this
+    # GPU: 805 M cpx per step, generated on the device outside the timed region.
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4)
+    shape4 = (64, 3, 2048, 2048)
+    a4 = torch.rand(shape4, device=dev, generator=gen)
+    b4 = (a4 + 0.1 * torch.randn(shape4, device=dev, generator=gen)).clamp_(0.0, 1.0)
+    a4.requires_grad_(True)
+
+    def step4(i):
+        v = fb.fused_ssim(a4, b4)
+        v.backward()
+        a4.grad = None
+
+    for i in range(2):
+        step4(i)
+    t4 = event_time(step4, 5)
+    n4 = a4.numel()
+    out["batch_2048"] = {"workload": "64x3x2048x2048 fp32, padding same, train, fwd+bwd, whole "
+                                     "batch on one GPU", "value": n4 / (t4 * 1e-3) / 1e6,
+                         "unit": "Mpix/s", "ms_per_step": t4, "steps": 5,
+                         "roof_ms": (FWD_BYTES_F32 + BWD_BYTES_F32) * n4 / (hbm * 1e9) * 1e3}
+    out["batch_2048"]["frac_roofline"] = out["batch_2048"]["roof_ms"] / t4
+    del a4, b4
     torch.cuda.synchronize()
     out["cpu_baseline"] = cpu_baseline(steps=2, budget_s=15.0)
     return out
