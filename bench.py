@@ -369,6 +369,30 @@ def measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, step_ms
     out["e2e"] = {"value": n / (t_e * 1e-3) / 1e6, "unit": "Mpix/s", "ms_per_step": t_e,
                   "h2d_bytes_per_step": 2 * n * 4, "d2h_bytes_per_step": 4, "steps": e_iters}
 
+    # The 3DGS photometric loss 0.8*L1 + 0.2*(1-SSIM) at 1080p: fused (one forward and one
+    # backward kernel) against the same loss composed from fused_ssim and torch's L1.
+    def gs_fused(i):
+        x, y = pairs[i % N_ROT]
+        v = fb.l1_dssim_loss(x, y, lambda_dssim=0.2)
+        v.backward()
+        x.grad = None
+
+    def gs_composed(i):
+        x, y = pairs[i % N_ROT]
+        v = 0.8 * (x - y).abs().mean() + 0.2 * (1.0 - fb.fused_ssim(x, y))
+        v.backward()
+        x.grad = None
+
+    g_iters = max(10, min(K, 300))
+    for i in range(warm):
+        gs_fused(i)
+        gs_composed(i)
+    t_gf = event_time(gs_fused, g_iters)
+    t_gc = event_time(gs_composed, g_iters)
+    out["l1_dssim_1080p"] = {"workload": "1x3x1080x1920 fp32, 0.8*L1 + 0.2*(1-SSIM), fwd+bwd",
+                             "fused_ms_per_step": t_gf, "composed_ms_per_step": t_gc,
+                             "fused_value": n / (t_gf * 1e-3) / 1e6, "unit": "Mpix/s"}
+
     # FP16 autocast workload (8x3x1024^2, valid padding) on this GPU
     del parts
     h16 = [synthetic.make_pair("fp16_1024_valid", seed=77 + k) for k in range(N_ROT)]

@@ -24,12 +24,14 @@ from .functional import (  # noqa: F401
     check_compatibility,
     fused_ssim,
     get_build_info,
+    l1_dssim_loss,
     ssim,
 )
 
 __all__ = [
     # Primary API
     "fused_ssim",
+    "l1_dssim_loss",
     # pytorch-msssim compatible API
     "ssim",
     "SSIM",

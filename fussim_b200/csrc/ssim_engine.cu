@@ -439,7 +439,8 @@ int fssim_fusedssim_fp16_backward(int window_size, float C1, float C2, const uin
 
 size_t fssim_forward_workspace_bytes(int64_t B) {
   if (B <= 0) return 256;
-  return 256 + static_cast<size_t>(B) * sizeof(unsigned long long);
+  // ticket, then B SSIM and B L1 fixed-point accumulators
+  return 256 + 2 * static_cast<size_t>(B) * sizeof(unsigned long long);
 }
 
 }  // extern "C"
@@ -473,7 +474,7 @@ int forward_impl(const fssim_forward_args* a, const fssim::DpParams* dp, cudaStr
     if (a->reduce != FSSIM_REDUCE_NONE) {
       const int64_t n_out = a->reduce == FSSIM_REDUCE_SCALAR ? 1 : a->B;
       if (n_out > 0) {
-        fill_kernel<<<1, 128, 0, stream>>>(a->out, n_out, 0.f * a->out_scale);
+        fill_kernel<<<1, 128, 0, stream>>>(a->out, n_out, 0.f * a->out_scale + a->out_offset);
         const int e = launch_error("fill launch");
         if (e) return e;
       }
@@ -504,11 +505,15 @@ int forward_impl(const fssim_forward_args* a, const fssim::DpParams* dp, cudaStr
   if (a->reduce != FSSIM_REDUCE_NONE) {
     p.ticket = static_cast<unsigned*>(a->workspace);
     p.acc = reinterpret_cast<unsigned long long*>(static_cast<char*>(a->workspace) + 256);
+    p.acc_l1 = p.acc + a->B;
   }
   p.g = make_geometry(a->B, a->C, a->H, a->W);
   p.C1 = a->C1;
   p.C2 = a->C2;
   p.out_scale = a->out_scale;
+  p.l1_weight = a->l1_weight;
+  p.out_offset = a->out_offset;
+  p.l1 = (a->l1_weight != 0.f && a->reduce != FSSIM_REDUCE_NONE) ? 1 : 0;
   p.valid = a->valid ? 1 : 0;
   p.clamp = a->clamp ? 1 : 0;
   p.reduce = a->reduce;
@@ -677,6 +682,7 @@ int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
   p.grad = a->grad;
   p.g = make_geometry(a->B, a->C, a->H, a->W);
   p.chain_scale = a->chain_scale;
+  p.l1_scale = a->l1_scale;
   p.grad_per_image = a->grad_out_per_image ? 1 : 0;
   p.grad_dtype = a->grad_dtype;
   p.aligned16 = (a->W % static_cast<int64_t>(16 / PE) == 0) && aligned(p.p0, 16) &&
@@ -706,8 +712,8 @@ int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
 // by the library or by the caller, who still passes the inputs and outputs.
 //
 // What that costs:
-//  * every GPU that loads this library holds the array (256 B + 8 B per image for
-//    FSSIM_NOALLOC_MAX_IMAGES images, about 33 KiB) until the process exits;
+//  * every GPU that loads this library holds the array (256 B + 16 B per image for
+//    FSSIM_NOALLOC_MAX_IMAGES images, about 65 KiB) until the process exits;
 //  * the array is shared by all calls: two calls whose kernels overlap on the GPU (on
 //    different streams or from different host threads) race on it and return wrong
 //    sums, so such calls must be serialised;
@@ -720,7 +726,7 @@ int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
 namespace {
 
 constexpr size_t kNoAllocScratchBytes =
-    256 + sizeof(unsigned long long) * static_cast<size_t>(FSSIM_NOALLOC_MAX_IMAGES);
+    256 + 2 * sizeof(unsigned long long) * static_cast<size_t>(FSSIM_NOALLOC_MAX_IMAGES);
 
 // In host code this name is only a stand-in for the symbol, never a device address: the
 // address handed to the kernel comes from cudaGetSymbolAddress in noalloc_scratch().

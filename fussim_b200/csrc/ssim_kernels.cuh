@@ -561,6 +561,24 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
   return ((red[0] + red[1]) + red[2]) + red[3];
 }
 
+// Deterministic block sums of two doubles at once (red holds 8 doubles).
+__device__ __forceinline__ void block_sum2(double& a, double& b, double* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) {
+    red[warp] = a;
+    red[4 + warp] = b;
+  }
+  __syncthreads();
+  a = ((red[0] + red[1]) + red[2]) + red[3];
+  b = ((red[4] + red[5]) + red[6]) + red[7];
+}
+
 // Vertical 2*HALO+1 tap sum of column pairs for 8 consecutive output rows: rows k..k+2HALO
 // of `v` feed output k (reference order: pairs d = 1..HALO, centre last).
 template <int HALO, bool HW_>
@@ -675,9 +693,12 @@ struct FwdParams {
   float* out;            // reduction outputs
   double* image_sums;    // optional FP64 per-image sums
   unsigned long long* acc;  // B fixed-point accumulators (workspace)
+  unsigned long long* acc_l1;  // B more for the L1 sums (workspace, used when l1)
   unsigned* ticket;         // last-CTA ticket (workspace)
   Geometry g;
   float C1, C2, out_scale;
+  float l1_weight, out_offset;  // out = out_scale*sum(ssim) + l1_weight*sum|x-y| + out_offset
+  int l1;                       // accumulate sum |x - y| (fused L1 term)
   int valid, clamp, reduce, mask_partials, aligned16, pair_ok, use_tma;
 };
 
@@ -710,9 +731,14 @@ struct FwdConfig {
 // Horizontal pass of the forward: for staged row i and output columns 8j..8j+7 compute the
 // moments sum w*X, w*X^2, w*Y, w*Y^2, w*XY (order of the reference's xconv features), or
 // with MERGED sum w*X, w*(X^2+Y^2), w*Y, w*XY, as four column pairs.
+// With l1 set it also adds |x - y| of the task's 8 centre pixels to l1_sum, for staged rows
+// [l1_i0, l1_i1) and the strip's first l1_cols columns (each image pixel is counted by
+// exactly one task of one step).
 template <int HALO, typename TIn, int MAXR, bool MERGED>
 __device__ __forceinline__ void fwd_hpass(const TIn* sx, const TIn* sy, float* ring, int nh,
-                                          int hdst, const Taps2<HALO, sizeof(TIn) == 2>& T) {
+                                          int hdst, const Taps2<HALO, sizeof(TIn) == 2>& T,
+                                          bool l1, int l1_i0, int l1_i1, int l1_cols,
+                                          float& l1_sum) {
   constexpr int SP = StagePitch<TIn>::value;
   constexpr int RP = RingPitch<MERGED ? 4 : 5>::value;
   constexpr int HA = (sizeof(TIn) == 2 || HALO > 4) ? 8 : 4;  // aligned left extent
@@ -735,6 +761,14 @@ __device__ __forceinline__ void fwd_hpass(const TIn* sx, const TIn* sy, float* r
           XX.a[q] = mul2(X.a[q], X.a[q]);
           XY.a[q] = mul2(X.a[q], Y.a[q]);
           YY.a[q] = MERGED ? fma2(Y.a[q], Y.a[q], XX.a[q]) : mul2(Y.a[q], Y.a[q]);
+        }
+        if (l1 && i >= l1_i0 && i < l1_i1) {
+          const int nc = l1_cols - 8 * j;  // centre columns of the task inside the image
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 dv = sub2(X.pr(HA + 2 * q), Y.pr(HA + 2 * q));
+            l1_sum += (2 * q < nc ? fabsf(dv.x) : 0.f) + (2 * q + 1 < nc ? fabsf(dv.y) : 0.f);
+          }
         }
         float* dst = ring + (hdst + i) * RP + 8 * j;
 #pragma unroll
@@ -785,7 +819,7 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   unsigned char* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
   TIn* stg = reinterpret_cast<TIn*>(smem);
   float* ring = reinterpret_cast<float*>(smem + Cfg::kStageBytes);
-  __shared__ double red[4];
+  __shared__ double red[8];
   __shared__ unsigned s_last;
   __shared__ uint64_t bar;
 
@@ -825,6 +859,8 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   }
   unsigned phase = 0;
   double run_sum = 0.0;
+  double run_l1 = 0.0;
+  const bool l1 = a.l1 != 0;
 
   while (cur.n) {
     bool timed_out = false;
@@ -848,8 +884,18 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
     const bool early = tma && nxt.n && !cur.first && !nxt.first;
     nxt.slot = early ? (cur.slot ^ kRows) : 0;
     if (early) issue(nxt);
-    fwd_hpass<HALO, TIn, SROWS, MERGED>(stg + cur.slot * SP, stg + (SROWS + cur.slot) * SP, ring,
-                                        cur.nh(), cur.hdst(), T);
+    float step_l1 = 0.f;
+    {
+      // L1 term: staged rows of the CTA's own output rows [segment start, t_end)
+      const int l1_i0 = cur.first ? HALO : 0;
+      const int l1_hi = cur.t_end - cur.h0();
+      const int l1_i1 = l1_hi < cur.nh() ? l1_hi : cur.nh();
+      const int l1_cols = static_cast<int>(g.W) - cur.strip * kStrip;
+      fwd_hpass<HALO, TIn, SROWS, MERGED>(stg + cur.slot * SP, stg + (SROWS + cur.slot) * SP,
+                                          ring, cur.nh(), cur.hdst(), T, l1, l1_i0, l1_i1,
+                                          l1_cols, step_l1);
+    }
+    run_l1 += static_cast<double>(step_l1);
     __syncthreads();
     if (nxt.n && !early) {
       if (!tma) {
@@ -979,11 +1025,21 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
 
     if (a.reduce && cur.last()) {
       // end of a column run: fold its sum into the image's fixed-point accumulator
-      const double s = block_sum(run_sum, red);
+      double s = run_sum, s1 = run_l1;
+      if (l1) {
+        block_sum2(s, s1, red);
+      } else {
+        s = block_sum(s, red);
+      }
       run_sum = 0.0;
+      run_l1 = 0.0;
       if (threadIdx.x == 0) {
         const long long q = __double2ll_rn(s * kFixScale);
         atomicAdd(a.acc + cur.img, static_cast<unsigned long long>(q));
+        if (l1) {
+          const long long q1 = __double2ll_rn(s1 * kFixScale);
+          atomicAdd(a.acc_l1 + cur.img, static_cast<unsigned long long>(q1));
+        }
       }
     }
     __syncthreads();
@@ -1001,18 +1057,28 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  double local = 0.0;
+  double local = 0.0, local_l1 = 0.0;
   for (int b = threadIdx.x; b < g.B; b += kThreads) {
     const long long q = static_cast<long long>(atomicExch(a.acc + b, 0ull));
     const double s = static_cast<double>(q) * (1.0 / kFixScale);
+    double s1 = 0.0;
+    if (l1) s1 = static_cast<double>(static_cast<long long>(atomicExch(a.acc_l1 + b, 0ull))) *
+                 (1.0 / kFixScale);
     if (a.image_sums) a.image_sums[b] = s;
-    if (a.reduce == 2) a.out[b] = static_cast<float>(s * static_cast<double>(a.out_scale));
+    if (a.reduce == 2)
+      a.out[b] = static_cast<float>(s * static_cast<double>(a.out_scale) +
+                                    s1 * static_cast<double>(a.l1_weight) +
+                                    static_cast<double>(a.out_offset));
     local += s;
+    local_l1 += s1;
   }
   if (a.reduce == 1) {
-    const double total = block_sum(local, red);
+    double total = local, total_l1 = local_l1;
+    block_sum2(total, total_l1, red);
     if (threadIdx.x == 0) {
-      a.out[0] = static_cast<float>(total * static_cast<double>(a.out_scale));
+      a.out[0] = static_cast<float>(total * static_cast<double>(a.out_scale) +
+                                    total_l1 * static_cast<double>(a.l1_weight) +
+                                    static_cast<double>(a.out_offset));
       if (a.dp.world > 0) dp_publish(a.dp, total);
     }
   }
@@ -1033,6 +1099,7 @@ struct BwdParams {
   void* grad;             // output
   Geometry g;
   float chain_scale;
+  float l1_scale;         // fused L1 term: adds l1_scale * upstream * sign(x - y) (0: none)
   int grad_per_image, grad_dtype, aligned16, pair_ok, use_tma;
 };
 
@@ -1235,8 +1302,11 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
 
     if (r0 < cur.n) {
       float2 chain = splat(a.chain_scale);
+      float2 l1c = splat(a.l1_scale);
       if (!DLMAP && a.grad_out) {
-        chain = mul2(chain, splat(a.grad_out[a.grad_per_image ? cur.img : 0]));
+        const float2 up = splat(a.grad_out[a.grad_per_image ? cur.img : 0]);
+        chain = mul2(chain, up);
+        l1c = mul2(l1c, up);
       }
       float2 res[3][kRPT];
 #pragma unroll
@@ -1252,6 +1322,16 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
       for (int k = 0; k < kRPT; ++k) {
         gv[k] = fma2(yin[k], res[2][k], fma2(mul2(two, xin[k]), res[1][k], res[0][k]));
         if (!DLMAP) gv[k] = mul2(gv[k], chain);
+      }
+      if (!DLMAP && a.l1_scale != 0.f) {
+        // d|x - y|/dx = sign(x - y), 0 where x == y (torch's abs backward)
+#pragma unroll
+        for (int k = 0; k < kRPT; ++k) {
+          const float2 dv = sub2(xin[k], yin[k]);
+          const float2 sg = make_float2(dv.x > 0.f ? 1.f : (dv.x < 0.f ? -1.f : 0.f),
+                                        dv.y > 0.f ? 1.f : (dv.y < 0.f ? -1.f : 0.f));
+          gv[k] = fma2(sg, l1c, gv[k]);
+        }
       }
       auto store_grad = [&](auto* base) {
         auto* gp = base + plane_off;

@@ -202,7 +202,7 @@ torch::Tensor workspace_for(const torch::Tensor& like, int64_t B) {
 std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward_impl(
     torch::Tensor img1, torch::Tensor img2, int window_size, double C1, double C2, bool valid,
     bool clamp, bool train, int reduce, bool half_partials, double out_scale,
-    const fssim_dp_args* dp) {
+    double l1_weight, double out_offset, const fssim_dp_args* dp) {
   check_window(window_size);
   check_cuda_4d(img1, "img1");
   check_cuda_4d(img2, "img2");
@@ -239,6 +239,8 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward_impl(
   args.C1 = static_cast<float>(C1);
   args.C2 = static_cast<float>(C2);
   args.out_scale = static_cast<float>(out_scale);
+  args.l1_weight = static_cast<float>(l1_weight);
+  args.out_offset = static_cast<float>(out_offset);
   args.img1 = a.data_ptr();
   args.img2 = b.data_ptr();
   args.ssim_map = nullptr;
@@ -254,9 +256,10 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward_impl(
 
 std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward(
     torch::Tensor img1, torch::Tensor img2, int window_size, double C1, double C2, bool valid,
-    bool clamp, bool train, int reduce, bool half_partials, double out_scale) {
+    bool clamp, bool train, int reduce, bool half_partials, double out_scale, double l1_weight,
+    double out_offset) {
   return loss_forward_impl(img1, img2, window_size, C1, C2, valid, clamp, train, reduce,
-                           half_partials, out_scale, nullptr);
+                           half_partials, out_scale, l1_weight, out_offset, nullptr);
 }
 
 // ---- batch-sharded loss: peer mailboxes over CUDA IPC ----
@@ -279,7 +282,7 @@ std::tuple<torch::Tensor, torch::Tensor> loss_forward_dp(
     std::vector<int64_t> mailboxes) {
   const fssim_dp_args d = make_dp(world, rank, seq, mailboxes);
   auto r = loss_forward_impl(img1, img2, window_size, C1, C2, valid, false, train, 1, false,
-                             out_scale, &d);
+                             out_scale, 0.0, 0.0, &d);
   return {std::get<0>(r), std::get<1>(r)};
 }
 
@@ -320,9 +323,10 @@ void ipc_close_handle(int64_t ptr) {
   check_status(fssim_ipc_close_handle(reinterpret_cast<void*>(ptr)));
 }
 
-torch::Tensor loss_backward(torch::Tensor grad_out, torch::Tensor img1, torch::Tensor img2,
-                            torch::Tensor partials, int window_size, bool per_image,
-                            double chain_scale, int grad_dtype) {
+torch::Tensor loss_backward_impl(torch::Tensor grad_out, torch::Tensor img1,
+                                 torch::Tensor img2, torch::Tensor partials, int window_size,
+                                 bool per_image, double chain_scale, int grad_dtype,
+                                 double l1_scale) {
   check_window(window_size);
   check_cuda_4d(img1, "img1");
   const at::cuda::OptionalCUDAGuard guard(img1.device());
@@ -353,9 +357,17 @@ torch::Tensor loss_backward(torch::Tensor grad_out, torch::Tensor img1, torch::T
   args.grad_out = go.data_ptr<float>();
   args.grad_out_per_image = per_image ? 1 : 0;
   args.chain_scale = static_cast<float>(chain_scale);
+  args.l1_scale = static_cast<float>(l1_scale);
   args.grad = grad.data_ptr();
   check_status(fssim_backward(&args, current_stream()));
   return grad;
+}
+
+torch::Tensor loss_backward(torch::Tensor grad_out, torch::Tensor img1, torch::Tensor img2,
+                            torch::Tensor partials, int window_size, bool per_image,
+                            double chain_scale, int grad_dtype) {
+  return loss_backward_impl(grad_out, img1, img2, partials, window_size, per_image,
+                            chain_scale, grad_dtype, 0.0);
 }
 
 std::string version() { return fssim_version(); }
@@ -368,7 +380,8 @@ struct FusedLossFn : public torch::autograd::Function<FusedLossFn> {
   static torch::Tensor forward(torch::autograd::AutogradContext* ctx, torch::Tensor img1,
                                torch::Tensor img2, double C1, double C2, int64_t window_size,
                                bool valid, bool clamp, int64_t reduce, bool half,
-                               double scale, double chain_scale) {
+                               double scale, double chain_scale, double l1_weight,
+                               double out_offset, double l1_scale) {
     torch::Tensor a, b;
     if (half) {
       a = img1.scalar_type() == at::kHalf ? img1 : img1.to(at::kHalf);
@@ -378,11 +391,13 @@ struct FusedLossFn : public torch::autograd::Function<FusedLossFn> {
       b = img2.scalar_type() == img1.scalar_type() ? img2 : img2.to(img1.scalar_type());
     }
     auto r = loss_forward_impl(a, b, static_cast<int>(window_size), C1, C2, valid, clamp, true,
-                               static_cast<int>(reduce), false, scale, nullptr);
+                               static_cast<int>(reduce), false, scale, l1_weight, out_offset,
+                               nullptr);
     ctx->save_for_backward({a, b, std::get<1>(r)});
     ctx->saved_data["ws"] = window_size;
     ctx->saved_data["per_image"] = reduce == 2;
     ctx->saved_data["chain"] = chain_scale;
+    ctx->saved_data["l1"] = l1_scale;
     ctx->saved_data["gdt"] = static_cast<int64_t>(dtype_code(img1.scalar_type()));
     return std::get<0>(r);
   }
@@ -390,22 +405,26 @@ struct FusedLossFn : public torch::autograd::Function<FusedLossFn> {
   static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
                                                  torch::autograd::variable_list grads) {
     const auto saved = ctx->get_saved_variables();
-    auto grad = loss_backward(grads[0], saved[0], saved[1], saved[2],
-                              static_cast<int>(ctx->saved_data["ws"].toInt()),
-                              ctx->saved_data["per_image"].toBool(),
-                              ctx->saved_data["chain"].toDouble(),
-                              static_cast<int>(ctx->saved_data["gdt"].toInt()));
-    return {grad,            torch::Tensor(), torch::Tensor(), torch::Tensor(),
-            torch::Tensor(), torch::Tensor(), torch::Tensor(), torch::Tensor(),
-            torch::Tensor(), torch::Tensor(), torch::Tensor()};
+    auto grad = loss_backward_impl(grads[0], saved[0], saved[1], saved[2],
+                                   static_cast<int>(ctx->saved_data["ws"].toInt()),
+                                   ctx->saved_data["per_image"].toBool(),
+                                   ctx->saved_data["chain"].toDouble(),
+                                   static_cast<int>(ctx->saved_data["gdt"].toInt()),
+                                   ctx->saved_data["l1"].toDouble());
+    torch::autograd::variable_list out(14);
+    out[0] = grad;
+    return out;
   }
 };
 
+// out = scale * sum(ssim) + l1_weight * sum|img1 - img2| + out_offset (per image when
+// reduce == 2); d(out)/d(map) = chain_scale, and l1_scale * sign(img1 - img2) per pixel.
 torch::Tensor fused_loss(torch::Tensor img1, torch::Tensor img2, double C1, double C2,
                          int64_t window_size, bool valid, bool clamp, int64_t reduce, bool half,
-                         double scale, double chain_scale) {
+                         double scale, double chain_scale, double l1_weight, double out_offset,
+                         double l1_scale) {
   return FusedLossFn::apply(img1, img2, C1, C2, window_size, valid, clamp, reduce, half, scale,
-                            chain_scale);
+                            chain_scale, l1_weight, out_offset, l1_scale);
 }
 
 }  // namespace
@@ -416,7 +435,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fusedssim_fp16", &fusedssim_fp16);
   m.def("fusedssim_fp16_train", &fusedssim_fp16_train);
   m.def("fusedssim_fp16_backward", &fusedssim_fp16_backward);
-  m.def("loss_forward", &loss_forward);
+  m.def("loss_forward", &loss_forward, py::arg("img1"), py::arg("img2"),
+        py::arg("window_size"), py::arg("C1"), py::arg("C2"), py::arg("valid"),
+        py::arg("clamp"), py::arg("train"), py::arg("reduce"), py::arg("half_partials"),
+        py::arg("out_scale"), py::arg("l1_weight") = 0.0, py::arg("out_offset") = 0.0);
   m.def("loss_backward", &loss_backward);
   m.def("fused_loss", &fused_loss);
   m.def("loss_forward_dp", &loss_forward_dp);

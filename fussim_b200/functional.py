@@ -191,7 +191,7 @@ def _reduce(img1, img2, C1, C2, window_size, valid, clamp, reduce, train, half):
         scale = _inv(_count(img1.shape, window_size, valid, reduce == _REDUCE_PER_IMAGE))
         chain = scale if scale != float("inf") else 0.0
         return ext.fused_loss(img1, img2, C1, C2, window_size, valid, clamp, reduce, half,
-                              scale, chain)
+                              scale, chain, 0.0, 0.0, 0.0)
     a, b = _kernel_inputs(img1, img2, half)
     scale = _inv(_count(a.shape, window_size, valid, reduce == _REDUCE_PER_IMAGE))
     out, _, _ = ext.loss_forward(a, b, window_size, C1, C2, valid, clamp, False, reduce, False,
@@ -268,6 +268,66 @@ def fused_ssim(
         img1, img2 = _float_path_inputs(img1, img2)
     return _reduce(img1, img2, C1, C2, window_size, padding == "valid", False, _REDUCE_SCALAR,
                    train, half)
+
+
+def l1_dssim_loss(
+    img1: torch.Tensor,
+    img2: torch.Tensor,
+    lambda_dssim: float = 0.2,
+    padding: str = "same",
+    window_size: int = 11,
+) -> torch.Tensor:
+    """The 3D Gaussian Splatting photometric loss in one fused forward and one backward:
+
+        (1 - lambda_dssim) * mean|img1 - img2| + lambda_dssim * (1 - fused_ssim(img1, img2))
+
+    (the combination in the reference's tests/test_amp.py:223-227). The L1 mean runs over
+    every pixel; the SSIM mean follows ``padding`` as in ``fused_ssim``. The forward kernel
+    sums |img1 - img2| alongside the SSIM map and the backward kernel adds the L1 gradient
+    (sign(img1 - img2) / N, 0 where equal), so neither image is read again for the L1 term.
+    Differentiable with respect to img1; under autocast the FP16 path runs (the L1 term is
+    then computed from the half-rounded images). Returns a 0-d float32 tensor.
+    """
+    if not torch.cuda.is_available():
+        raise RuntimeError("CUDA is not available. l1_dssim_loss requires a CUDA-capable GPU.")
+    if not img1.is_cuda or not img2.is_cuda:
+        raise RuntimeError("img1 and img2 must be on a CUDA device")
+    if img1.device != img2.device:
+        raise RuntimeError("img1 and img2 must be on the same device.")
+    if img1.shape != img2.shape:
+        raise ValueError(
+            "img1 and img2 must have the same shape.\n"
+            f"img1 shape: {img1.shape}, img2 shape: {img2.shape}"
+        )
+    if len(img1.shape) != 4:
+        raise ValueError(
+            f"Expected 4D tensor (B, C, H, W), but got {len(img1.shape)}D tensor "
+            f"with shape {img1.shape}"
+        )
+    if padding not in ALLOWED_PADDING:
+        raise ValueError(f"padding must be one of {ALLOWED_PADDING}, but got '{padding}'")
+    if window_size not in SUPPORTED_WINDOW_SIZES:
+        raise ValueError(f"window_size must be one of {SUPPORTED_WINDOW_SIZES}, got {window_size}")
+    lam = float(lambda_dssim)
+    if not 0.0 <= lam <= 1.0:
+        raise ValueError(f"lambda_dssim must be in [0, 1], got {lambda_dssim}")
+    half = torch.is_autocast_enabled()
+    if not half:
+        img1, img2 = _float_path_inputs(img1, img2)
+    valid = padding == "valid"
+    ext = _ensure_cuda_extension()
+    inv_ssim = _inv(_count(img1.shape, window_size, valid, False))
+    inv_all = _inv(img1.numel())
+    ssim_scale = -lam * inv_ssim if inv_ssim != float("inf") else 0.0
+    l1_scale = (1.0 - lam) * inv_all if inv_all != float("inf") else 0.0
+    if torch.is_grad_enabled() and img1.requires_grad:
+        return ext.fused_loss(img1, img2, 0.01**2, 0.03**2, window_size, valid, False,
+                              _REDUCE_SCALAR, half, ssim_scale, ssim_scale, l1_scale, lam,
+                              l1_scale)
+    a, b = _kernel_inputs(img1, img2, half)
+    out, _, _ = ext.loss_forward(a, b, window_size, 0.01**2, 0.03**2, valid, False, False,
+                                 _REDUCE_SCALAR, False, ssim_scale, l1_scale, lam)
+    return out
 
 
 def ssim(

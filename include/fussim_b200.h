@@ -152,6 +152,12 @@ typedef struct fssim_forward_args {
    * calls on the same stream; calls that may overlap on the GPU need separate workspaces. */
   void* workspace;
   size_t workspace_bytes;
+  /* Fused L1 term (the 3DGS loss (1-l)*mean|x-y| + l*(1-SSIM)): with l1_weight != 0 (and a
+   * reduction) the forward also sums |img1 - img2| over every pixel of each image and
+   * writes out = out_scale * sum(ssim) + l1_weight * sum|img1 - img2| + out_offset (per
+   * image for FSSIM_REDUCE_PER_IMAGE). Zero-initialise both for plain SSIM. */
+  float l1_weight;
+  float out_offset;
 } fssim_forward_args;
 
 typedef struct fssim_backward_args {
@@ -169,6 +175,9 @@ typedef struct fssim_backward_args {
   int32_t grad_out_per_image;
   float chain_scale;
   void* grad;             /* B*C*H*W of grad_dtype */
+  /* Fused L1 term: adds l1_scale * grad_out[.] * sign(img1 - img2) (0 where equal) to every
+   * pixel's gradient. 0 for plain SSIM. */
+  float l1_scale;
 } fssim_backward_args;
 
 /* Bytes of workspace fssim_forward needs for a batch of B images. */
@@ -188,7 +197,7 @@ int fssim_backward(const fssim_backward_args* args, fssim_stream_t stream);
 /* fssim_forward for callers that cannot allocate GPU memory (no counterpart in the
  * reference). Same arguments and outputs as fssim_forward; args->workspace and
  * args->workspace_bytes are ignored. The reduction scratch is a fixed array in the
- * library's device memory (about 33 KiB, held by every GPU that loads the library until
+ * library's device memory (about 65 KiB, held by every GPU that loads the library until
  * exit), so nothing is allocated per call: for plugins whose host owns all device memory,
  * fixed-budget real-time loops, and bindings without a device allocator. Limits: at most
  * FSSIM_NOALLOC_MAX_IMAGES images (larger B returns FSSIM_ERR_WORKSPACE); all calls share

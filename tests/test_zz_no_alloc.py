@@ -40,6 +40,7 @@ class ForwardArgs(ctypes.Structure):
         ("img1", ctypes.c_void_p), ("img2", ctypes.c_void_p), ("ssim_map", ctypes.c_void_p),
         ("partials", ctypes.c_void_p), ("out", ctypes.c_void_p), ("image_sums", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t),
+        ("l1_weight", ctypes.c_float), ("out_offset", ctypes.c_float),
     ]
 
 
