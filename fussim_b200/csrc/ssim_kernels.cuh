@@ -8,10 +8,11 @@
 // splits [0, LT) into G equal contiguous ranges, so every CTA gets the same number of
 // rows whatever the image shape. A CTA walks its range in steps of up to 16 output rows:
 //
-//   stage   input rows of the step (64 + 16 columns, zero outside the image) -> smem,
-//           issued with cp.async one step ahead so the copy overlaps the previous step;
-//   H-pass  horizontal Gaussian of every staged row -> a smem ring of moment rows
-//           (5 moments forward, 3 partials backward);
+//   stage   input rows of the step (64 + 16 columns, zero outside the image) -> smem by
+//           TMA boxes (cp.async where the layout does not allow TMA), issued one step
+//           ahead so the copy overlaps the previous step;
+//   H-pass  horizontal Gaussian of every staged row -> a smem ring of moment rows (4 maps
+//           in the fused forward, 5 in the map-producing one, 3 partials backward);
 //   V-pass  vertical Gaussian of the ring for the step's 16 x 64 outputs, then the
 //           per-pixel epilogue (SSIM + partials, or the gradient).
 //
@@ -579,7 +580,7 @@ __device__ __forceinline__ void block_sum2(double& a, double& b, double* red) {
   b = ((red[4] + red[5]) + red[6]) + red[7];
 }
 
-// Vertical 2*HALO+1 tap sum of column pairs for 8 consecutive output rows: rows k..k+2HALO
+// Vertical 2*HALO+1 tap sum of column pairs for kRPT consecutive output rows: rows k..k+2HALO
 // of `v` feed output k (reference order: pairs d = 1..HALO, centre last).
 template <int HALO, bool HW_>
 __device__ __forceinline__ void vsumR(const float2 (&v)[kRPT + 2 * HALO], float2 (&o)[kRPT],
@@ -682,7 +683,7 @@ __global__ void __launch_bounds__(32) dp_gather_kernel(const DpParams dp, float 
 }
 
 struct FwdParams {
-  CUtensorMap tmap[2];   // img1, img2 as (W, H, planes), boxes of 8 rows (when use_tma)
+  CUtensorMap tmap[2];   // img1, img2 as (W, H, planes), boxes of kBoxRows rows (when use_tma)
   DpParams dp;           // sharded loss: publish the batch sum to every rank (dp.world > 0)
   const void* img1;
   const void* img2;
@@ -905,7 +906,7 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
       }
     }
 
-    // ---- V-pass + epilogue: rows r0..r0+7 of the step, columns 2*lane, 2*lane+1 ----
+    // ---- V-pass + epilogue: rows r0..r0+kRPT-1 of the step, columns 2*lane, 2*lane+1 ----
     if (r0 < cur.n) {
       float2 res[NM][kRPT];
 #pragma unroll
