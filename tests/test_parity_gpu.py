@@ -22,7 +22,10 @@ from tests import refpath
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(1, 2, 40, 45), (2, 1, 37, 19), (1, 3, 64, 67), (2, 3, 96, 256), (1, 1, 5, 7)]
+# Widths that are not multiples of 8 stage with cp.async; the others with TMA boxes
+# (including boxes that run past the bottom and right edges, and images smaller than a box).
+SHAPES = [(1, 2, 40, 45), (2, 1, 37, 19), (1, 3, 64, 67), (2, 3, 96, 256), (1, 1, 5, 7),
+          (2, 3, 37, 64), (1, 1, 5, 8), (1, 2, 130, 200)]
 WINDOWS = (7, 9, 11)
 
 
