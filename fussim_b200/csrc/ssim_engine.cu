@@ -141,8 +141,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // FP32 or FP16 elements, boxes of kBoxRows rows x one staged row pitch of columns,
 // zero fill outside. False (the kernels then stage with cp.async) when the layout does not
 // meet the copy unit's rules: 16-byte aligned base, row pitch a multiple of 16 bytes.
-bool encode_rows(CUtensorMap* m, const void* base, size_t esize, const fssim::Geometry& g,
-                 int box_w = 0) {
+bool encode_rows(CUtensorMap* m, const void* base, size_t esize, const fssim::Geometry& g) {
   const PFN_cuTensorMapEncodeTiled_v12000 fn = tensor_map_encoder();
   if (!fn || !base || !aligned(base, 16)) return false;
   if ((static_cast<size_t>(g.W) * esize) % 16 != 0) return false;
@@ -153,9 +152,9 @@ bool encode_rows(CUtensorMap* m, const void* base, size_t esize, const fssim::Ge
                         static_cast<cuuint64_t>(planes)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(g.W) * esize,
                            static_cast<cuuint64_t>(g.HW) * esize};
-  const int w = box_w > 0 ? box_w
-                          : (f32 ? fssim::StagePitch<float>::value : fssim::StagePitch<__half>::value);
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(w), static_cast<cuuint32_t>(fssim::kBoxRows), 1u};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(f32 ? fssim::StagePitch<float>::value
+                                                   : fssim::StagePitch<__half>::value),
+                       static_cast<cuuint32_t>(fssim::kBoxRows), 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUresult r =
       fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
@@ -170,14 +169,10 @@ void set_fwd_tma(fssim::FwdParams& p, size_t esize) {
   p.use_tma = encode_rows(&p.tmap[0], p.img1, esize, p.g) &&
               encode_rows(&p.tmap[1], p.img2, esize, p.g);
 }
-// Backward: the three partial maps (and dL/dmap) with halo columns, and the two images as
-// 16 x 64 boxes of the step's output pixels.
-void set_bwd_tma(fssim::BwdParams& p, size_t pesize, size_t esize) {
+void set_bwd_tma(fssim::BwdParams& p, size_t pesize) {
   bool ok = encode_rows(&p.tmap[0], p.p0, pesize, p.g) &&
             encode_rows(&p.tmap[1], p.p1, pesize, p.g) &&
-            encode_rows(&p.tmap[2], p.p2, pesize, p.g) &&
-            encode_rows(&p.tmap[4], p.img1, esize, p.g, fssim::kStrip) &&
-            encode_rows(&p.tmap[5], p.img2, esize, p.g, fssim::kStrip);
+            encode_rows(&p.tmap[2], p.p2, pesize, p.g);
   if (ok && p.dl) ok = encode_rows(&p.tmap[3], p.dl, sizeof(float), p.g);
   p.use_tma = ok;
 }
@@ -343,7 +338,7 @@ int compat_backward(int ws, const TIn* img1, const TIn* img2, const float* dl, c
                 aligned(p2, 16);
   p.pair_ok = (W % 2 == 0) && aligned(img1, 2 * sizeof(TIn)) && aligned(img2, 2 * sizeof(TIn)) &&
               aligned(grad, 8);
-  set_bwd_tma(p, sizeof(float), sizeof(TIn));
+  set_bwd_tma(p, sizeof(float));
   return dispatch_bwd<TIn, float, true>(ws, p, stream);
 }
 
@@ -694,7 +689,7 @@ int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
                 aligned(p.p1, 16) && aligned(p.p2, 16);
   p.pair_ok = (a->W % 2 == 0) && aligned(a->img1, 2 * E) && aligned(a->img2, 2 * E) &&
               aligned(a->grad, 2 * GE);
-  set_bwd_tma(p, PE, E);
+  set_bwd_tma(p, PE);
   const int ws = a->window_size;
   cudaStream_t s = stream;
   if (a->dtype == FSSIM_F32) return dispatch_bwd<float, float, false>(ws, p, s);

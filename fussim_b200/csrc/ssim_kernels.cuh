@@ -341,14 +341,6 @@ __device__ __forceinline__ float2 load2(const T* base, I idx, bool pair, bool in
   return make_float2(in0 ? to_f(base[idx]) : 0.f, in1 ? to_f(base[idx + 1]) : 0.f);
 }
 
-// A column pair from shared memory (8-byte / 4-byte aligned), as floats.
-__device__ __forceinline__ float2 lds2(const float* p) {
-  return *reinterpret_cast<const float2*>(p);
-}
-__device__ __forceinline__ float2 lds2(const __half* p) {
-  return __half22float2(*reinterpret_cast<const __half2*>(p));
-}
-
 // ---------------------------------------------------------------------------------------
 // Geometry and step sequencing
 // ---------------------------------------------------------------------------------------
@@ -374,7 +366,6 @@ struct Step {
   int t_end;      // end row of the CTA's part of this column run
   int rest;       // strip-rows of the CTA's range after that part
   int slot;       // first staging row of the step (0 or kRows)
-  int islot;      // backward: image staging slot of the step (alternates 0, 1)
   bool first;     // first step of a run part: it also computes the top halo rows
   __device__ __forceinline__ int h0() const { return first ? t - HALO : t + HALO; }  // first moment row
   __device__ __forceinline__ int nh() const { return first ? n + 2 * HALO : n; }     // moment rows
@@ -418,7 +409,6 @@ __device__ __forceinline__ Step<HALO> first_step(int64_t beg, int64_t end, const
   s.t_end = s.t + static_cast<int>(seg);
   s.rest = static_cast<int>(len - seg);
   s.slot = 0;
-  s.islot = 0;
   s.first = true;
   s.n = static_cast<int>(seg) < kRows ? static_cast<int>(seg) : kRows;
   return s;
@@ -1099,8 +1089,7 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
 // Backward kernel
 // ---------------------------------------------------------------------------------------
 struct BwdParams {
-  CUtensorMap tmap[6];    // p0, p1, p2 (TP), dl (FP32): staged rows with halo columns;
-                          // img1, img2 (TIn): the step's 16 x 64 output pixels (when use_tma)
+  CUtensorMap tmap[4];    // p0, p1, p2 (TP) and dl (FP32) as (W, H, planes) (when use_tma)
   const void* img1;
   const void* img2;
   const void* p0;         // partials (TP)
@@ -1129,10 +1118,8 @@ struct BwdConfig {
   static constexpr size_t kDlBytes =
       DLMAP ? static_cast<size_t>(kSRows) * StagePitch<float>::value * sizeof(float) : 0;
   static constexpr size_t kRingBytes = static_cast<size_t>(kMaxR) * kRP * sizeof(float);
-  // the epilogue's image pairs, staged with the step: [2 slots][img1, img2][kRows][kStrip]
-  static constexpr size_t kImgBytes = 2ull * 2 * kRows * kStrip * sizeof(TIn);
   // + 128: the dynamic shared memory base is rounded up to 128 bytes for the TMA boxes
-  static constexpr size_t kSmem = kStageBytes + kDlBytes + kImgBytes + kRingBytes + 128;
+  static constexpr size_t kSmem = kStageBytes + kDlBytes + kRingBytes + 128;
   static constexpr int kFit = static_cast<int>((228 * 1024) / (kSmem + 1024));
   // 3 CTAs/SM: the backward gains more from the larger register budget (up to 170) than
   // it loses in occupancy (measured at 1080p: 37.9 us against 38.9 us at 4 CTAs/SM)
@@ -1201,9 +1188,7 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
   unsigned char* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
   TP* stg = reinterpret_cast<TP*>(smem);
   float* sdl = reinterpret_cast<float*>(smem + Cfg::kStageBytes);
-  TIn* simg = reinterpret_cast<TIn*>(smem + Cfg::kStageBytes + Cfg::kDlBytes);
-  float* ring =
-      reinterpret_cast<float*>(smem + Cfg::kStageBytes + Cfg::kDlBytes + Cfg::kImgBytes);
+  float* ring = reinterpret_cast<float*>(smem + Cfg::kStageBytes + Cfg::kDlBytes);
   __shared__ uint64_t bar;
 
   const Geometry& g = a.g;
@@ -1227,26 +1212,19 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
   }
   __syncthreads();
   Step<HALO> cur = first_step<HALO>(beg, end, g);
-  if (tma && threadIdx.x < 6) prefetch_tensormap(a.tmap + threadIdx.x);
+  if (tma && threadIdx.x < (DLMAP ? 4 : 3)) prefetch_tensormap(a.tmap + threadIdx.x);
   grid_dependency_wait();
   grid_launch_dependents();
   // TMA staging of a step by warp 0: lane 0 posts the byte count, the lanes issue the boxes
-  constexpr unsigned kImgStepBytes = 2u * kRows * kStrip * sizeof(TIn);
   auto issue = [&](const Step<HALO>& st) {
     if (warp == 0) {
       if (lane == 0)
         mbar_arrive_expect_tx(&bar, tma_step_bytes<TP, 3>(st.nh()) +
-                                        (DLMAP ? tma_step_bytes<float, 1>(st.nh()) : 0u) +
-                                        kImgStepBytes);
+                                        (DLMAP ? tma_step_bytes<float, 1>(st.nh()) : 0u));
       stage_tma_lanes<TP, 3, SROWS>(stg, a.tmap, st, &bar, 0);
-      const int nbox = (st.nh() + kBoxRows - 1) / kBoxRows;
-      if (DLMAP) stage_tma_lanes<float, 1, SROWS>(sdl, a.tmap + 3, st, &bar, 3 * nbox);
-      // the step's output pixels of img1 and img2, one 16 x 64 box each
-      const int li = lane - (DLMAP ? 4 : 3) * nbox;
-      if (li == 0 || li == 1) {
-        fence_proxy_async_smem();
-        tma_load_3d(simg + ((st.islot * 2 + li) * kRows) * kStrip, a.tmap + 4 + li,
-                    st.strip * kStrip, st.t, st.plane, &bar);
+      if (DLMAP) {
+        const int nbox = (st.nh() + kBoxRows - 1) / kBoxRows;
+        stage_tma_lanes<float, 1, SROWS>(sdl, a.tmap + 3, st, &bar, 3 * nbox);
       }
     }
   };
@@ -1286,7 +1264,7 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
     // plane base + 32-bit in-plane offsets (planes < 2^31 elements)
     const int off0 = (cur.t + r0) * W + gx0;
     float2 xin[kRPT], yin[kRPT];
-    if (!tma) {
+    {
       const TIn* x_pl = img1 + plane_off;
       const TIn* y_pl = img2 + plane_off;
       if (fast) {
@@ -1311,7 +1289,6 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
     Step<HALO> nxt = next_step<HALO>(cur, g);
     const bool early = tma && nxt.n && !cur.first && !nxt.first;
     nxt.slot = early ? (cur.slot ^ kRows) : 0;
-    nxt.islot = cur.islot ^ 1;
     if (early) issue(nxt);
     bwd_hpass<HALO, TIn, TP, DLMAP, SROWS>(stg + cur.slot * Cfg::kSP,
                                            sdl + cur.slot * StagePitch<float>::value, ring,
@@ -1342,16 +1319,6 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
         for (int q = 0; q < kRPT + 2 * HALO; ++q)
           v[q] = *reinterpret_cast<const float2*>(ring + (r0 + q) * RP + m * kStrip + 2 * lane);
         vsumR<HALO, HW_>(v, res[m], T);
-      }
-      if (tma) {
-        // the image pairs arrived with the step's staging (zero outside the image)
-        const TIn* sx = simg + (cur.islot * 2 * kRows + r0) * kStrip + 2 * lane;
-        const TIn* sy = sx + kRows * kStrip;
-#pragma unroll
-        for (int k = 0; k < kRPT; ++k) {
-          xin[k] = lds2(sx + k * kStrip);
-          yin[k] = lds2(sy + k * kStrip);
-        }
       }
       float2 gv[kRPT];
 #pragma unroll
