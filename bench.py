@@ -54,7 +54,7 @@ BWD_FLOPS = 2 * 3 * 2 * 11 + 6        # 3 partial maps x 2 passes x 11 MACs, com
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each kernel on
 # this workload, from one ncu capture (profiles/ssim_fwd_bwd_1080p_fp32.md; the capture
 # flushes L2 before each launch, so it is the cold-L2 figure).
-NCU_TRAFFIC_BYTES = {"fwd": 60.70e6 + 27.22e6, "bwd": 172.88e6 + 15.12e6}
+NCU_TRAFFIC_BYTES = {"fwd": 60.75e6 + 27.58e6, "bwd": 172.90e6 + 15.77e6}
 
 
 def load_peaks():
