@@ -381,7 +381,7 @@ struct FusedLossFn : public torch::autograd::Function<FusedLossFn> {
                                torch::Tensor img2, double C1, double C2, int64_t window_size,
                                bool valid, bool clamp, int64_t reduce, bool half,
                                double scale, double chain_scale, double l1_weight,
-                               double out_offset, double l1_scale) {
+                               double out_offset, double l1_scale, const fssim_dp_args* dp) {
     torch::Tensor a, b;
     if (half) {
       a = img1.scalar_type() == at::kHalf ? img1 : img1.to(at::kHalf);
@@ -392,7 +392,12 @@ struct FusedLossFn : public torch::autograd::Function<FusedLossFn> {
     }
     auto r = loss_forward_impl(a, b, static_cast<int>(window_size), C1, C2, valid, clamp, true,
                                static_cast<int>(reduce), false, scale, l1_weight, out_offset,
-                               nullptr);
+                               dp);
+    if (dp) {
+      // sharded loss: out = scale * (sum over every rank's shard), formed on this GPU
+      check_status(fssim_dp_gather(dp, static_cast<float>(scale),
+                                   std::get<0>(r).data_ptr<float>(), current_stream()));
+    }
     ctx->save_for_backward({a, b, std::get<1>(r)});
     ctx->saved_data["ws"] = window_size;
     ctx->saved_data["per_image"] = reduce == 2;
@@ -411,7 +416,7 @@ struct FusedLossFn : public torch::autograd::Function<FusedLossFn> {
                                    ctx->saved_data["chain"].toDouble(),
                                    static_cast<int>(ctx->saved_data["gdt"].toInt()),
                                    ctx->saved_data["l1"].toDouble());
-    torch::autograd::variable_list out(14);
+    torch::autograd::variable_list out(15);
     out[0] = grad;
     return out;
   }
@@ -424,7 +429,20 @@ torch::Tensor fused_loss(torch::Tensor img1, torch::Tensor img2, double C1, doub
                          double scale, double chain_scale, double l1_weight, double out_offset,
                          double l1_scale) {
   return FusedLossFn::apply(img1, img2, C1, C2, window_size, valid, clamp, reduce, half, scale,
-                            chain_scale, l1_weight, out_offset, l1_scale);
+                            chain_scale, l1_weight, out_offset, l1_scale,
+                            static_cast<const fssim_dp_args*>(nullptr));
+}
+
+// The fused loss of this rank's shard of a batch sharded over several GPUs: the value is
+// the mean over every rank's shard (peer mailboxes, fssim_forward_dp + fssim_dp_gather),
+// the gradient is local (d(out)/d(map) = scale = 1 / global count).
+torch::Tensor fused_loss_dp(torch::Tensor img1, torch::Tensor img2, int64_t window_size,
+                            bool valid, bool half, double scale, double chain_scale,
+                            int64_t world, int64_t rank, int64_t seq,
+                            std::vector<int64_t> mailboxes) {
+  const fssim_dp_args d = make_dp(world, rank, seq, mailboxes);
+  return FusedLossFn::apply(img1, img2, 0.01 * 0.01, 0.03 * 0.03, window_size, valid, false,
+                            int64_t{1}, half, scale, chain_scale, 0.0, 0.0, 0.0, &d);
 }
 
 }  // namespace
@@ -441,6 +459,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_scale"), py::arg("l1_weight") = 0.0, py::arg("out_offset") = 0.0);
   m.def("loss_backward", &loss_backward);
   m.def("fused_loss", &fused_loss);
+  m.def("fused_loss_dp", &fused_loss_dp);
   m.def("loss_forward_dp", &loss_forward_dp);
   m.def("dp_gather", &dp_gather);
   m.def("dp_mailbox_alloc", &dp_mailbox_alloc);

@@ -172,7 +172,17 @@ def fused_ssim_dp(img1, img2, padding="same", train=True, window_size=11, group=
     half = torch.is_autocast_enabled()
     train = train and torch.is_grad_enabled() and img1.requires_grad
     works: list = []
-    if train:
+    mb = _mailboxes_for(group, img1.device) if (train and img1.is_cuda) else None
+    if mb is not None:
+        # peer path: the C++ autograd function of the extension (forward publishes and
+        # gathers the shard sums, backward is local)
+        ext = F._ensure_cuda_extension()
+        mb.seq += 1
+        out = ext.fused_loss_dp(img1, img2, window_size, valid, half, scale,
+                                scale if scale != float("inf") else 0.0, mb.world, mb.rank,
+                                mb.seq, mb.ptrs)
+        works.append(_Done())
+    elif train:
         out = _ShardedSSIM.apply(img1, img2, window_size, valid, half, scale, group, works)
     else:
         a, b = F._kernel_inputs(img1, img2, half)
