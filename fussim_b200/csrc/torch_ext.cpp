@@ -202,7 +202,7 @@ torch::Tensor workspace_for(const torch::Tensor& like, int64_t B) {
 std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward_impl(
     torch::Tensor img1, torch::Tensor img2, int window_size, double C1, double C2, bool valid,
     bool clamp, bool train, int reduce, bool half_partials, double out_scale,
-    double l1_weight, double out_offset, const fssim_dp_args* dp) {
+    double l1_weight, double out_offset, const fssim_dp_args* dp, bool with_sums = true) {
   check_window(window_size);
   check_cuda_4d(img1, "img1");
   check_cuda_4d(img2, "img2");
@@ -222,7 +222,10 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward_impl(
             : torch::empty({0}, a.options().dtype(at::kFloat));
   auto out = reduce == 1 ? torch::empty({}, a.options().dtype(at::kFloat))
                          : torch::empty({B}, a.options().dtype(at::kFloat));
-  auto sums = torch::empty({B}, a.options().dtype(at::kDouble));
+  // the per-image FP64 sums are returned by the loss_forward binding; the autograd path
+  // does not use them and skips the allocation
+  auto sums = with_sums ? torch::empty({B}, a.options().dtype(at::kDouble))
+                        : torch::Tensor();
   auto ws = workspace_for(a, B);
   fssim_forward_args args{};
   args.dtype = dt;
@@ -246,7 +249,7 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward_impl(
   args.ssim_map = nullptr;
   args.partials = train ? partials.data_ptr() : nullptr;
   args.out = out.data_ptr<float>();
-  args.image_sums = sums.data_ptr<double>();
+  args.image_sums = with_sums ? sums.data_ptr<double>() : nullptr;
   args.workspace = ws.data_ptr();
   args.workspace_bytes = static_cast<size_t>(ws.numel()) * 8;
   check_status(dp ? fssim_forward_dp(&args, dp, current_stream())
@@ -392,7 +395,7 @@ struct FusedLossFn : public torch::autograd::Function<FusedLossFn> {
     }
     auto r = loss_forward_impl(a, b, static_cast<int>(window_size), C1, C2, valid, clamp, true,
                                static_cast<int>(reduce), false, scale, l1_weight, out_offset,
-                               dp);
+                               dp, /*with_sums=*/false);
     if (dp) {
       // sharded loss: out = scale * (sum over every rank's shard), formed on this GPU
       check_status(fssim_dp_gather(dp, static_cast<float>(scale),
