@@ -108,3 +108,8 @@ def test_cabi_host_only_paths():
     assert f(11, 1e-4, 9e-4, None, None, 0, 3, 8, 8, 1, None, None, None, None, None) == 0
     # negative sizes are a shape error
     assert f(11, 1e-4, 9e-4, None, None, -1, 3, 8, 8, 1, None, None, None, None, None) == 2
+    # the reserved-SM count is host state: negative counts are an argument error
+    lib.fssim_set_reserved_sms.argtypes = [ctypes.c_int]
+    assert lib.fssim_set_reserved_sms(-1) == 7  # FSSIM_ERR_ARGUMENT
+    assert lib.fssim_last_error() == b"reserved SM count must be >= 0"
+    assert lib.fssim_set_reserved_sms(0) == 0
