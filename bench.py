@@ -1,26 +1,31 @@
 #!/usr/bin/env python
 """fwd+bwd SSIM throughput on B200 — one JSON line on rank 0.
 
-Workload (per GPU): the 3DGS training-step shape, 1x3x1080x1920 FP32 render/ground-truth
-pair (seeded synthetic blob field + 3x3 box blur + noise), padding "same", window 11,
-train=True: ``loss = fused_ssim(img1, img2); loss.backward()`` through the public API.
-With N GPUs (torchrun) every rank holds its own 1080p pair (weak scaling); the global mean
-is formed by the forward kernels publishing their sums to every rank's mailbox over NVLink
-and a one-warp gather kernel per rank (no collective call in the step).
+Headline workload (per GPU): the 3DGS training-step shape, a 1x3x1080x1920 FP32
+render/ground-truth pair (seeded synthetic blob field + 3x3 box blur + noise), padding
+"same", window 11, train=True: ``loss = fused_ssim(img1, img2); loss.backward()`` through
+the public API. With N GPUs (torchrun) every rank holds its own 1080p pair (weak scaling);
+the global mean is formed by the forward kernels publishing their sums to every rank's
+mailbox over NVLink and a one-warp gather kernel per rank (no collective call in the step).
 
 Reported:
-* value      B*C*H*W/s of all ranks over the max-over-ranks device time (Mpix/s, the
-             reference's convention); inputs resident in HBM; 4 rotating input pairs
-             (200 MB per rank, > 126 MB L2) so no step starts with its inputs in L2.
+* value      B*C*H*W/s of all ranks over the max-over-ranks device time of K back-to-back
+             steps (Mpix/s, the reference's convention); inputs resident in HBM; 4 rotating
+             input pairs (200 MB per rank, > 126 MB L2) so no step starts with its inputs
+             in L2. The launch queue is filled before the first timed step (a GPU sleep
+             ahead of it), so the figure is the GPU's step rate; ``host_us_per_step`` is the
+             host's enqueue cost of one step, measured separately.
 * e2e        the same step through the public API with host (pinned) inputs: H2D copy of
              both images, fwd+bwd, D2H of the loss, every step.
 * roofline   the dominant kernel timed alone with CUDA events on its stream; achieved =
-             algorithmic bytes or FLOPs per launch / launch time (see DESIGN.md).
+             algorithmic bytes or FLOPs per launch / launch time.
+* batch_2048 the 64x3x2048^2 FP32 batch sharded over the N ranks (64/N images each).
+* fp16       FP16 autocast against FP32 on the same configurations (1080p same padding,
+             8x3x1024^2 valid padding).
 * cpu_baseline  the reference test suite's conv2d SSIM formula (fwd+bwd, FP32, all host
-             threads) on a bounded sample of the same workload.
-* fp16       the 8x3x1024^2 FP16 'valid' autocast workload on one GPU.
+             threads) on the full 1080p frame.
 
-``--impl reference`` prints the reference arm: the conv2d formula on the host cores.
+``--impl reference`` prints the reference arm: the same conv2d formula on the host cores.
 """
 
 from __future__ import annotations
@@ -31,7 +36,7 @@ import os
 import statistics
 import subprocess
 import sys
-import threading
+import tempfile
 import time
 
 import torch
@@ -41,7 +46,6 @@ sys.path.insert(0, ROOT)
 
 METRIC = "fwd+bwd SSIM Mpix/s (FP32, FP16) at 1080p RGB, 1/2/4/8 B200; % of roofline"
 SHAPE = (1, 3, 1080, 1920)
-FP16_SHAPE = (8, 3, 1024, 1024)
 N_ROT = 4
 
 # Algorithmic work per channel-pixel (cpx): bytes a kernel must move at minimum, and FP32
@@ -52,9 +56,11 @@ FWD_FLOPS = 2 * 5 * 2 * 11 + 3 + 30   # 5 moments x 2 passes x 11 MACs, 3 produc
 BWD_FLOPS = 2 * 3 * 2 * 11 + 6        # 3 partial maps x 2 passes x 11 MACs, combine + chain
 
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each kernel on
-# this workload, from one ncu capture (profiles/ssim_fwd_bwd_1080p_fp32.md; the capture
-# flushes L2 before each launch, so it is the cold-L2 figure).
+# the 1080p workload, from one ncu capture of this kernel version (ncu flushes L2 before each
+# captured launch, so these are cold-L2 figures).
 NCU_TRAFFIC_BYTES = {"fwd": 60.75e6 + 27.58e6, "bwd": 172.90e6 + 15.77e6}
+NCU_TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:ssim_ -s 6 -c 2 "
+                      "python bench.py --steps 50 --warmup 3 --skip-extras")
 
 
 def load_peaks():
@@ -68,29 +74,36 @@ def load_peaks():
     return peaks
 
 
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 class ClockSampler:
-    """nvidia-smi samples of SM clock and clock-event reasons, filtered to a time window."""
+    """nvidia-smi samples of SM clock and clock-event reasons, written by the nvidia-smi
+    process straight to a file (no reader thread in this process), parsed after the run."""
 
     FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index):
-        self.rows = []
         self.proc = None
+        self.file = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+        self.marks = []
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-i", str(gpu_index), "-lms", "50"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
+                stdout=self.file, stderr=subprocess.DEVNULL)
         except (OSError, ValueError):
             self.proc = None
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append((time.time(), [c.strip() for c in line.split(",")]))
 
     def stop(self):
         if self.proc is not None:
@@ -99,12 +112,28 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        self.file.flush()
+
+    def _rows(self):
+        import datetime as dt
+
+        self.file.seek(0)
+        rows = []
+        for line in self.file.read().splitlines():
+            cols = [c.strip() for c in line.split(",")]
+            try:
+                t = dt.datetime.strptime(cols[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except (ValueError, IndexError):
+                continue
+            rows.append((t, cols))
+        return rows
 
     def summary(self, t0, t1):
-        inside = [r for t, r in self.rows if t0 <= t <= t1]
+        rows = self._rows()
+        inside = [r for t, r in rows if t0 - 0.05 <= t <= t1 + 0.05]
         window = "timed"
         if not inside:
-            inside = [r for _, r in self.rows]
+            inside = [r for _, r in rows]
             window = "warmup+timed (timed region shorter than the sampling period)"
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -117,6 +146,10 @@ class ClockSampler:
             for name, v in zip(names, r[5:9]):
                 if v.strip().lower() == "active":
                     reasons.add(name)
+        try:
+            os.unlink(self.file.name)
+        except OSError:
+            pass
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
@@ -133,43 +166,40 @@ def cpu_formula_step(a, b):
     return v.item()
 
 
-def cpu_baseline(steps, budget_s=20.0):
-    """Time the CPU formula on a bounded sample (row band) of the 1080p workload."""
+def cpu_baseline(steps, budget_s=60.0):
+    """Time the CPU formula on the full 1080p frame, all host threads; `steps` is capped so
+    the leg stays within about budget_s."""
     from fussim_b200 import synthetic
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     a, b = synthetic.make_pair("rgb_1080p")
-    # size the sample from one probe on a 120-row band so the whole run stays bounded
-    band = 120
     t = time.perf_counter()
-    cpu_formula_step(a[:, :, :band], b[:, :, :band])
-    per_row = (time.perf_counter() - t) / band
-    rows = int(max(32, min(SHAPE[2], budget_s / max(steps, 1) / max(per_row, 1e-9))))
-    sa, sb = a[:, :, :rows].contiguous(), b[:, :, :rows].contiguous()
-    cpu_formula_step(sa, sb)  # warm
+    cpu_formula_step(a, b)  # warm (and a probe of the step time)
+    probe = time.perf_counter() - t
+    steps = int(max(1, min(steps, budget_s / max(probe, 1e-3))))
     t = time.perf_counter()
     for _ in range(steps):
-        cpu_formula_step(sa, sb)
+        cpu_formula_step(a, b)
     dt = (time.perf_counter() - t) / steps
-    cpx = sa.numel()
+    cpx = a.numel()
     return {"value": cpx / dt / 1e6, "unit": "Mpix/s", "cores": threads, "kind": "port",
-            "sample": f"1x3x{rows}x1920 band of the 1080p pair per step, {steps} steps, "
-                      f"conv2d formula fwd+bwd FP32 ({cpx} cpx/step)",
-            "ms_per_step": dt * 1e3}
+            "cpu": cpu_model(),
+            "sample": f"the full 1x3x1080x1920 pair per step, {steps} steps, conv2d formula "
+                      f"fwd+bwd FP32 ({cpx} cpx/step)",
+            "ms_per_step": dt * 1e3, "steps": steps}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    steps = max(1, min(args.steps, 50))
-    base = cpu_baseline(steps)
+    base = cpu_baseline(max(1, args.steps))
     line = {"metric": METRIC, "value": base["value"], "unit": "Mpix/s", "n_gpus": args.gpus,
-            "steps": steps, "warmup": args.warmup, "ms_per_step": base["ms_per_step"],
+            "steps": base["steps"], "warmup": args.warmup, "ms_per_step": base["ms_per_step"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": "1x3x1080x1920 fp32 same train fwd+bwd (host sample)",
+            "config": {"workload": "1x3x1080x1920 fp32 same train fwd+bwd (host cores)",
                        "global_batch": 1, "window": 11, "padding": "same"},
             "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "Mpix/s", "h2d_bytes_per_step": 0,
@@ -177,10 +207,15 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def event_time(fn, iters, stream=None):
+def event_time(fn, iters, stream=None, prime_us=0.0):
+    """Device ms per call of fn over `iters` back-to-back calls (CUDA events on `stream`).
+    With prime_us > 0 a GPU sleep of about that long is queued ahead of the first event, so
+    the host enqueues the first calls before the GPU starts timing them."""
     s = torch.cuda.current_stream() if stream is None else stream
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    if prime_us > 0:
+        torch.cuda._sleep(int(prime_us * 2000))  # ~2000 cycles per microsecond
     e0.record(s)
     for i in range(iters):
         fn(i)
@@ -189,10 +224,23 @@ def event_time(fn, iters, stream=None):
     return e0.elapsed_time(e1) / iters  # ms per call
 
 
+def host_enqueue_us(fn, iters=30):
+    """Host wall time to enqueue one call of fn, with the GPU busy (a long sleep queued
+    first) so the launch queue never fills and no call waits for the device."""
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(iters * 400 * 2000))  # ~400 us of GPU sleep per call
+    t = time.perf_counter()
+    for i in range(iters):
+        fn(i)
+    dt = time.perf_counter() - t
+    torch.cuda.synchronize()
+    return dt / iters * 1e6
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
     ap.add_argument("--skip-extras", action="store_true", help="only the headline number")
@@ -240,23 +288,29 @@ def main():
         x.grad = None
         return v
 
+    def max_over_ranks(ms):
+        if world == 1:
+            return ms
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     for i in range(warm):
         step(i)
     torch.cuda.synchronize()
+    host_us = host_enqueue_us(step)
     sampler = ClockSampler(local)
     time.sleep(0.3)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t0 = time.time()
-    ms = event_time(step, K)
+    ms = event_time(step, K, prime_us=min(K, 100) * 150.0)
     t1 = time.time()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms)
     time.sleep(0.2)
     sampler.stop()
     clocks = sampler.summary(t0, t1)
@@ -265,6 +319,12 @@ def main():
     extras = {}
     if rank == 0 and not args.skip_extras:
         extras = measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, ms)
+    if not args.skip_extras:
+        # every rank takes part: the batch is sharded over the ranks
+        del pairs
+        torch.cuda.empty_cache()
+        extras["batch_2048"] = measure_batch_2048(fb, fdist, dev, world, rank, warm, peaks,
+                                                  max_over_ranks)
     if world > 1:
         fdist.release_mailboxes()
         dist.barrier()
@@ -280,8 +340,11 @@ def main():
                    "global_batch": world, "shape_per_gpu": list(SHAPE),
                    "parallelism": f"dp{world}" if world > 1 else "none",
                    "l2": "4 rotating input pairs per GPU (200 MB > 126 MB L2)",
+                   "timing": "CUDA events around K back-to-back steps, launch queue primed "
+                             "by a GPU sleep before the first event; max over ranks",
                    "rgb_mpix_per_s": value / 3.0},
-        "gpu_launches": 2 * K,
+        "host_us_per_step": host_us,
+        "gpu_launches": 2 * K + (K if world > 1 else 0),
         "clocks": clocks,
     }
     line.update(extras)
@@ -310,8 +373,8 @@ def measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, step_ms
     for i in range(warm):
         fwd(i)
         bwd(i)
-    t_f = event_time(fwd, iters)
-    t_b = event_time(bwd, iters)
+    t_f = event_time(fwd, iters, prime_us=3000)
+    t_b = event_time(bwd, iters, prime_us=3000)
     hbm = peaks["hbm_gbs"]
     fp32_peak = 148 * 128 * 2 * peaks["sm_max_mhz"] * 1e6 / 1e12  # TFLOP/s, nominal
     kern = {
@@ -330,13 +393,13 @@ def measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, step_ms
     d = kern[dom]
     if d["bound"] == "hbm":
         roof = {"bound": "hbm", "achieved": d["gbs"], "peak": hbm, "unit": "GB/s",
-                "frac": d["gbs"] / hbm, "traffic": None}
+                "frac": d["gbs"] / hbm}
     else:
         roof = {"bound": "fp32", "achieved": d["tflops"], "peak": fp32_peak, "unit": "TFLOP/s",
-                "frac": d["tflops"] / fp32_peak, "traffic": None}
+                "frac": d["tflops"] / fp32_peak}
     roof["traffic"] = NCU_TRAFFIC_BYTES[dom]
     roof.update(kernel=f"ssim_{dom}_kernel", launch_us=d["us"], traffic_unit="bytes per launch",
-                algorithmic_bytes=d["bytes"],
+                traffic_source=NCU_TRAFFIC_SOURCE, algorithmic_bytes=d["bytes"],
                 peak_source=("hbm: MEASURED_PEAKS.json (measured)" if peaks["source"] == "measured"
                              else "hbm: fallback") + "; fp32: 148 SMs x 128 lanes x 2 x sm_max_mhz")
     out["roofline"] = roof
@@ -345,9 +408,11 @@ def measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, step_ms
     t_step_roof = max((FWD_BYTES_F32 + BWD_BYTES_F32) * n / (hbm * 1e9),
                       (FWD_FLOPS + BWD_FLOPS) * n / (fp32_peak * 1e12))
     out["step_roofline"] = {"roof_us": t_step_roof * 1e6, "kernels_us": (t_f + t_b) * 1e3,
+                            "api_step_us": step_ms * 1e3,
                             "frac_kernels": t_step_roof * 1e3 / (t_f + t_b),
                             "frac_api_step": t_step_roof * 1e3 / step_ms,
                             "bound": "hbm", "bytes_per_cpx": FWD_BYTES_F32 + BWD_BYTES_F32}
+    del parts
 
     # e2e through the public API with host buffers
     pinned = [(a.pin_memory(), b.pin_memory()) for a, b in host]
@@ -387,63 +452,92 @@ def measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, step_ms
     for i in range(warm):
         gs_fused(i)
         gs_composed(i)
-    t_gf = event_time(gs_fused, g_iters)
-    t_gc = event_time(gs_composed, g_iters)
+    t_gf = event_time(gs_fused, g_iters, prime_us=3000)
+    t_gc = event_time(gs_composed, g_iters, prime_us=3000)
     out["l1_dssim_1080p"] = {"workload": "1x3x1080x1920 fp32, 0.8*L1 + 0.2*(1-SSIM), fwd+bwd",
                              "fused_ms_per_step": t_gf, "composed_ms_per_step": t_gc,
                              "fused_value": n / (t_gf * 1e-3) / 1e6, "unit": "Mpix/s"}
 
-    # FP16 autocast workload (8x3x1024^2, valid padding) on this GPU
-    del parts
-    h16 = [synthetic.make_pair("fp16_1024_valid", seed=77 + k) for k in range(N_ROT)]
-    p16 = [(a.to(dev).requires_grad_(True), b.to(dev)) for a, b in h16]
-
-    def step16(i):
-        x, y = p16[i % N_ROT]
-        with torch.autocast("cuda"):
-            v = fb.fused_ssim(x, y, padding="valid")
-        v.backward()
-        x.grad = None
-
-    i16 = max(10, min(K, 300))
-    for i in range(warm):
-        step16(i)
-    t16 = event_time(step16, i16)
-    n16 = p16[0][0].numel()
-    v16 = n16 / (t16 * 1e-3) / 1e6
-    v32 = n / (step_ms * 1e-3) / 1e6
-    out["fp16"] = {"workload": "8x3x1024x1024 fp16 inputs, autocast, padding valid, train, "
-                               "fwd+bwd", "value": v16, "unit": "Mpix/s", "ms_per_step": t16,
-                   "ratio_vs_fp32_1080p": v16 / v32, "steps": i16}
-    torch.cuda.synchronize()
-    del p16
-    # The data-parallel batch config (64x3x2048^2 FP32, U[0,1] + N(0, 0.1^2)) whole on this
-    # GPU: 805 M cpx per step, generated on the device outside the timed region.
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(4)
-    shape4 = (64, 3, 2048, 2048)
-    a4 = torch.rand(shape4, device=dev, generator=gen)
-    b4 = (a4 + 0.1 * torch.randn(shape4, device=dev, generator=gen)).clamp_(0.0, 1.0)
-    a4.requires_grad_(True)
-
-    def step4(i):
-        v = fb.fused_ssim(a4, b4)
-        v.backward()
-        a4.grad = None
-
-    for i in range(2):
-        step4(i)
-    t4 = event_time(step4, 5)
-    n4 = a4.numel()
-    out["batch_2048"] = {"workload": "64x3x2048x2048 fp32, padding same, train, fwd+bwd, whole "
-                                     "batch on one GPU", "value": n4 / (t4 * 1e-3) / 1e6,
-                         "unit": "Mpix/s", "ms_per_step": t4, "steps": 5,
-                         "roof_ms": (FWD_BYTES_F32 + BWD_BYTES_F32) * n4 / (hbm * 1e9) * 1e3}
-    out["batch_2048"]["frac_roofline"] = out["batch_2048"]["roof_ms"] / t4
-    del a4, b4
-    torch.cuda.synchronize()
-    out["cpu_baseline"] = cpu_baseline(steps=2, budget_s=15.0)
+    out["fp16"] = measure_fp16(fb, synthetic, pairs, dev, K, warm, step_ms)
+    out["cpu_baseline"] = cpu_baseline(steps=3, budget_s=15.0)
     return out
+
+
+def measure_fp16(fb, synthetic, pairs, dev, K, warm, step_ms_fp32):
+    """FP16 autocast against FP32, each pair on the same configuration and inputs."""
+    iters = max(10, min(K, 300))
+
+    def run(pp, padding, half):
+        def st(i):
+            x, y = pp[i % len(pp)]
+            with torch.autocast("cuda", enabled=half):
+                v = fb.fused_ssim(x, y, padding=padding)
+            v.backward()
+            x.grad = None
+
+        for i in range(warm):
+            st(i)
+        return event_time(st, iters, prime_us=3000)
+
+    n1080 = pairs[0][0].numel()
+    t16_1080 = run(pairs, "same", True)
+    res = {"1080p_same": {"workload": "1x3x1080x1920, padding same, train, fwd+bwd",
+                          "fp32_ms": step_ms_fp32, "fp16_ms": t16_1080,
+                          "fp32_value": n1080 / (step_ms_fp32 * 1e-3) / 1e6,
+                          "fp16_value": n1080 / (t16_1080 * 1e-3) / 1e6,
+                          "fp16_over_fp32": step_ms_fp32 / t16_1080}}
+    # 8x3x1024^2 blob pairs, valid padding: FP32 inputs for both legs (autocast rounds them
+    # to FP16 inside the FP16 leg, as the reference does)
+    h = [synthetic.make_pair("fp16_1024_valid", seed=77 + k) for k in range(2)]
+    p = [(a.float().to(dev).requires_grad_(True), b.float().to(dev)) for a, b in h]
+    n = p[0][0].numel()
+    t32 = run(p, "valid", False)
+    t16 = run(p, "valid", True)
+    res["8x1024_valid"] = {"workload": "8x3x1024x1024 blob pairs, padding valid, train, fwd+bwd",
+                           "fp32_ms": t32, "fp16_ms": t16,
+                           "fp32_value": n / (t32 * 1e-3) / 1e6,
+                           "fp16_value": n / (t16 * 1e-3) / 1e6, "fp16_over_fp32": t32 / t16}
+    del p
+    torch.cuda.synchronize()
+    return res
+
+
+def measure_batch_2048(fb, fdist, dev, world, rank, warm, peaks, max_over_ranks):
+    """The 64x3x2048^2 FP32 batch (img1 ~ U[0,1], img2 = clamp(img1 + N(0, 0.1^2))) sharded
+    over the ranks, 64/N images each, generated on the device outside the timed region."""
+    per = 64 // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4 + 7919 * rank)
+    shape = (per, 3, 2048, 2048)
+    a = torch.rand(shape, device=dev, generator=gen)
+    b = (a + 0.1 * torch.randn(shape, device=dev, generator=gen)).clamp_(0.0, 1.0)
+    a.requires_grad_(True)
+
+    def st(i):
+        if world > 1:
+            v = fdist.fused_ssim_dp(a, b)
+        else:
+            v = fb.fused_ssim(a, b)
+        v.backward()
+        a.grad = None
+
+    for i in range(min(warm, 3)):
+        st(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    iters = 5
+    ms = max_over_ranks(event_time(st, iters))
+    n_total = 64 * 3 * 2048 * 2048
+    hbm = peaks["hbm_gbs"]
+    roof_ms = (FWD_BYTES_F32 + BWD_BYTES_F32) * n_total / world / (hbm * 1e9) * 1e3
+    del a, b
+    torch.cuda.empty_cache()
+    return {"workload": "64x3x2048x2048 fp32, padding same, train, fwd+bwd, sharded over "
+                        f"{world} GPU(s), {per} images each",
+            "value": n_total / (ms * 1e-3) / 1e6, "unit": "Mpix/s", "ms_per_step": ms,
+            "steps": iters, "n_gpus": world, "roof_ms_per_gpu": roof_ms,
+            "frac_roofline": roof_ms / ms}
 
 
 if __name__ == "__main__":

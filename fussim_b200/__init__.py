@@ -22,9 +22,11 @@ from .functional import (  # noqa: F401
     FusedSSIMMapFP16,
     __version__,
     check_compatibility,
+    check_device_errors,
     fused_ssim,
     get_build_info,
     l1_dssim_loss,
+    poll_device_error,
     ssim,
 )
 
@@ -42,5 +44,7 @@ __all__ = [
     "__version__",
     "get_build_info",
     "check_compatibility",
+    "check_device_errors",
+    "poll_device_error",
     "SUPPORTED_WINDOW_SIZES",
 ]

@@ -3,6 +3,7 @@
 // include/fussim_b200.h. No torch, no Python: any host language can bind this library.
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <atomic>
 #include <climits>
@@ -18,6 +19,16 @@
 namespace {
 
 thread_local std::string g_last_error;
+
+// NVTX range over an entry point's host-side work (argument checks and launches), so a
+// timeline tool shows the forward, backward and cross-GPU exchange by name. Without a tool
+// attached a push/pop costs a few nanoseconds.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 int fail(int code, const std::string& msg) {
   g_last_error = msg;
@@ -109,6 +120,11 @@ int kernel_occupancy(Kernel k, size_t smem, int (&cache)[64], std::mutex& mu, in
 // SMs the persistent grids leave free (fssim_set_reserved_sms), e.g. for a collective
 // that runs concurrently with a kernel of this library.
 std::atomic<int> g_reserved_sms{0};
+
+// Bound of a staging step's wait (polls) and of the sharded gather's wait (ns).
+constexpr long long kDefaultGatherTimeoutNs = 10ll * 1000 * 1000 * 1000;
+std::atomic<int> g_wait_limit{fssim::kWaitLimit};
+std::atomic<long long> g_gather_timeout_ns{kDefaultGatherTimeoutNs};
 
 int grid_size(const fssim::Geometry& g, int occ, int sms) {
   int use = sms - g_reserved_sms.load(std::memory_order_relaxed);
@@ -242,7 +258,9 @@ int launch_fwd(const fssim::FwdParams& p, cudaStream_t stream) {
   if (st) return st;
   const int grid = grid_size(p.g, occ, sms);
   if ((p.g.LT + grid - 1) / grid + 2 * p.g.H > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
-  const cudaError_t e = launch_pdl(k, grid, Cfg::kSmem, stream, p);
+  fssim::FwdParams q = p;
+  q.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
+  const cudaError_t e = launch_pdl(k, grid, Cfg::kSmem, stream, q);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();
     return fail(FSSIM_ERR_CUDA, std::string("ssim forward launch: ") + cudaGetErrorString(e));
@@ -263,7 +281,9 @@ int launch_bwd(const fssim::BwdParams& p, cudaStream_t stream) {
   if (st) return st;
   const int grid = grid_size(p.g, occ, sms);
   if ((p.g.LT + grid - 1) / grid + 2 * p.g.H > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
-  const cudaError_t e = launch_pdl(k, grid, Cfg::kSmem, stream, p);
+  fssim::BwdParams q = p;
+  q.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
+  const cudaError_t e = launch_pdl(k, grid, Cfg::kSmem, stream, q);
   if (e != cudaSuccess) {
     (void)cudaGetLastError();
     return fail(FSSIM_ERR_CUDA, std::string("ssim backward launch: ") + cudaGetErrorString(e));
@@ -399,6 +419,21 @@ int fssim_set_reserved_sms(int n) {
   return FSSIM_OK;
 }
 
+int fssim_set_staging_wait_limit(long long polls) {
+  g_last_error.clear();
+  const long long v = polls < 0 ? fssim::kWaitLimit : (polls > INT_MAX ? INT_MAX : polls);
+  g_wait_limit.store(static_cast<int>(v), std::memory_order_relaxed);
+  return FSSIM_OK;
+}
+
+int fssim_set_gather_timeout_us(long long us) {
+  g_last_error.clear();
+  const long long cap = LLONG_MAX / 1000;
+  const long long ns = us <= 0 ? kDefaultGatherTimeoutNs : (us > cap ? cap : us) * 1000;
+  g_gather_timeout_ns.store(ns, std::memory_order_relaxed);
+  return FSSIM_OK;
+}
+
 int fssim_poll_device_error(unsigned* code, int clear) {
   g_last_error.clear();
   if (!code) return fail(FSSIM_ERR_NULLPTR, "code is NULL");
@@ -420,6 +455,7 @@ int fssim_fusedssim(int window_size, float C1, float C2, const float* img1, cons
                     int64_t B, int64_t C, int64_t H, int64_t W, int train, float* ssim_map,
                     float* dm_dmu1, float* dm_dsigma1_sq, float* dm_dsigma12,
                     fssim_stream_t stream) {
+  NvtxRange range("fssim_fusedssim");
   return compat_forward<float>(window_size, C1, C2, img1, img2, B, C, H, W, train != 0, ssim_map,
                                dm_dmu1, dm_dsigma1_sq, dm_dsigma12, stream);
 }
@@ -431,6 +467,7 @@ int fssim_fusedssim_backward(int window_size, float C1, float C2, const float* i
                              fssim_stream_t stream) {
   (void)C1;
   (void)C2;  // the backward needs only the partials, as in the reference
+  NvtxRange range("fssim_fusedssim_backward");
   return compat_backward<float>(window_size, img1, img2, dL_dmap, dm_dmu1, dm_dsigma1_sq,
                                 dm_dsigma12, B, C, H, W, dL_dimg1, stream);
 }
@@ -492,6 +529,9 @@ int forward_impl(const fssim_forward_args* a, const fssim::DpParams* dp, cudaStr
   const int64_t N = a->B * a->C * a->H * a->W;
   if (a->reduce != FSSIM_REDUCE_NONE) {
     if (!a->out) return fail(FSSIM_ERR_NULLPTR, "out is required when reducing");
+    // an image's SSIM sum (|value| <= 1 per pixel) must fit the 2^28 fixed point in 63 bits
+    if (a->C * a->H * a->W > (int64_t{1} << 34))
+      return fail(FSSIM_ERR_SHAPE, "C*H*W must be <= 2^34 per image for the reductions");
     if (!a->workspace || a->workspace_bytes < fssim_forward_workspace_bytes(a->B))
       return fail(FSSIM_ERR_WORKSPACE, "workspace smaller than fssim_forward_workspace_bytes(B)");
     if (!aligned(a->workspace, 16)) return fail(FSSIM_ERR_WORKSPACE, "workspace must be 16-byte aligned");
@@ -579,6 +619,7 @@ int check_dp(const fssim_dp_args* d, fssim::DpParams* out) {
   p.world = d->world;
   p.rank = d->rank;
   p.seq = d->seq;
+  p.timeout_ns = static_cast<unsigned long long>(g_gather_timeout_ns.load(std::memory_order_relaxed));
   *out = p;
   return FSSIM_OK;
 }
@@ -588,6 +629,7 @@ int check_dp(const fssim_dp_args* d, fssim::DpParams* out) {
 extern "C" {
 
 int fssim_forward(const fssim_forward_args* a, fssim_stream_t stream) {
+  NvtxRange range("fssim_forward");
   g_last_error.clear();
   return forward_impl(a, nullptr, stream);
 }
@@ -655,6 +697,7 @@ int fssim_ipc_close_handle(void* peer_mailbox) {
 }
 
 int fssim_forward_dp(const fssim_forward_args* a, const fssim_dp_args* dp, fssim_stream_t stream) {
+  NvtxRange range("fssim_forward_dp");
   g_last_error.clear();
   if (!a) return fail(FSSIM_ERR_NULLPTR, "args is NULL");
   if (a->reduce != FSSIM_REDUCE_SCALAR) return fail(FSSIM_ERR_ARGUMENT, "fssim_forward_dp needs reduce = SCALAR");
@@ -669,6 +712,7 @@ int fssim_forward_dp(const fssim_forward_args* a, const fssim_dp_args* dp, fssim
 }
 
 int fssim_dp_gather(const fssim_dp_args* dp, float scale, float* out, fssim_stream_t stream) {
+  NvtxRange range("fssim_dp_gather");
   g_last_error.clear();
   if (!out) return fail(FSSIM_ERR_NULLPTR, "out is NULL");
   fssim::DpParams p{};
@@ -679,6 +723,7 @@ int fssim_dp_gather(const fssim_dp_args* dp, float scale, float* out, fssim_stre
 }
 
 int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
+  NvtxRange range("fssim_backward");
   g_last_error.clear();
   if (!a) return fail(FSSIM_ERR_NULLPTR, "args is NULL");
   int st = check_window(a->window_size);

@@ -48,7 +48,12 @@ constexpr int kRows = 16;             // output rows per step
 constexpr int kRPT = kRows / 4;       // output rows per thread in the V-pass (4 warps)
 constexpr int kLeft = 8;              // staged columns left of the strip (>= HALO, 16-byte aligned)
 constexpr int kInCols = kStrip + 2 * kLeft;  // 80 staged columns
-constexpr double kFixScale = 268435456.0;    // 2^28 fixed point for the sums
+// Fixed-point scales of the per-image sums. SSIM values lie in [-1, 1], so an image's SSIM
+// sum stays within 2^34 (the host rejects C*H*W > 2^34 for the reductions) and 2^28 fits it
+// in a signed 64-bit word. The L1 sum of |x - y| has no such bound; 2^20 leaves room for
+// image sums up to 2^43 (8.8e12) at an absolute resolution of 1e-6 per column run.
+constexpr double kFixScale = 268435456.0;    // 2^28: SSIM sums
+constexpr double kFixScaleL1 = 1048576.0;    // 2^20: L1 sums
 
 // Staged row pitch in elements. The pitch in 4-byte words is 4 * odd, so the 8 lanes of
 // a quarter warp reading 16 bytes each from 8 consecutive rows hit distinct banks.
@@ -168,7 +173,11 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // that complete on an mbarrier. This replaces 2-4 cp.async chunks per thread per staged
 // row and all their address arithmetic. Each copy reads this GPU's own memory into this CTA only.
 constexpr int kBoxRows = 16;  // one box per map for a regular step
-constexpr int kWaitLimit = 1 << 20;  // bounded mbarrier polls before a step reports failure
+// Bounded mbarrier polls before a step reports failure. The kernels take the limit of a
+// step's first wait as a parameter (the host default is this value; a limit of 0 makes
+// every TMA-staged step fail at once, which tests use to exercise the failure path). The
+// wait that drains a failed step's copies before the CTA leaves always uses this bound.
+constexpr int kWaitLimit = 1 << 20;
 
 // Device-side failure codes (OR-ed into g_device_error, read by fssim_poll_device_error).
 constexpr unsigned kErrStagingTimeout = 1u;
@@ -200,10 +209,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
       : "memory");
   return ok != 0;
 }
-// Wait for the mbarrier phase with the given parity to complete; false after kWaitLimit
-// polls (the caller reports the failure and leaves the kernel).
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
-  for (int i = 0; i < kWaitLimit; ++i)
+// Wait for the mbarrier phase with the given parity to complete; false after `limit` polls
+// (the caller reports the failure and stops its work).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity, int limit) {
+  for (int i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
@@ -616,7 +625,6 @@ __device__ __forceinline__ void vsumR(const float2 (&v)[kRPT + 2 * HALO], float2
 // seq+1 sum, which each rank publishes only after its own gather of step seq.
 constexpr int kMaxDpRanks = 8;
 constexpr unsigned kErrGatherTimeout = 2u;
-constexpr int kGatherPollLimit = 1 << 22;  // polls of 64 ns sleep: ~0.3 s before failing
 
 struct DpMailSlot {
   double sum;
@@ -628,7 +636,15 @@ struct DpParams {
   int world;                      // 0: not sharded
   int rank;
   unsigned long long seq;
+  unsigned long long timeout_ns;  // gather: give up after this long (device global timer)
 };
+
+// Nanoseconds of the device's global timer.
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ void dp_publish(const DpParams& dp, double sum) {
   const int set = static_cast<int>(dp.seq & 1ull);
@@ -649,7 +665,9 @@ __global__ void dp_publish_kernel(const DpParams dp, double sum) {
 }
 
 // One warp: lane r < world waits for slot [seq & 1][r] of this rank's mailbox, then lane 0
-// writes out[0] = scale * (sum of the world sums in rank order).
+// writes out[0] = scale * (sum of the world sums in rank order). The wait ends after
+// dp.timeout_ns of the device's global timer: out[0] is then NaN and bit 1 of the device
+// error flag is set.
 __global__ void __launch_bounds__(32) dp_gather_kernel(const DpParams dp, float scale, float* out) {
   const int lane = threadIdx.x;
   const int set = static_cast<int>(dp.seq & 1ull);
@@ -659,10 +677,10 @@ __global__ void __launch_bounds__(32) dp_gather_kernel(const DpParams dp, float 
     const DpMailSlot* slot = dp.mail[dp.rank] + set * dp.world + lane;
     const volatile unsigned long long* seqp =
         reinterpret_cast<const volatile unsigned long long*>(&slot->seq);
-    int i = 0;
-    while (*seqp != dp.seq && i < kGatherPollLimit) {
-      __nanosleep(64);
-      ++i;
+    const unsigned long long t0 = global_timer_ns();
+    while (*seqp != dp.seq) {
+      if (global_timer_ns() - t0 > dp.timeout_ns) break;
+      __nanosleep(128);
     }
     ok = (*seqp == dp.seq);
     __threadfence_system();
@@ -701,6 +719,7 @@ struct FwdParams {
   float l1_weight, out_offset;  // out = out_scale*sum(ssim) + l1_weight*sum|x-y| + out_offset
   int l1;                       // accumulate sum |x - y| (fused L1 term)
   int valid, clamp, reduce, mask_partials, aligned16, pair_ok, use_tma;
+  int wait_limit;               // polls of a step's staging wait before the step fails
 };
 
 // MERGED (the fused loss path): the SSIM value and its partials depend on the second moments
@@ -862,21 +881,25 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   double run_sum = 0.0;
   double run_l1 = 0.0;
   const bool l1 = a.l1 != 0;
+  bool failed = false;
 
   while (cur.n) {
     bool timed_out = false;
     if (tma) {
-      timed_out = !mbar_wait_bounded(&bar, phase);
+      timed_out = !mbar_wait_bounded(&bar, phase, a.wait_limit);
       phase ^= 1u;
     } else {
       cp_async_wait_all();
     }
     if (__syncthreads_or(timed_out)) {
       // staging did not complete: report it, give the copies in flight one more bounded
-      // wait so none lands after the CTA has exited, and leave
+      // wait so none lands after the CTA has exited, and stop; the CTA still takes its
+      // reduction ticket below, so the last CTA turns the outputs into NaN and leaves
+      // the workspace zeroed for the next call
       if (threadIdx.x == 0) atomicOr(&g_device_error, kErrStagingTimeout);
-      mbar_wait_bounded(&bar, phase ^ 1u);
-      return;
+      mbar_wait_bounded(&bar, phase ^ 1u, kWaitLimit);
+      failed = true;
+      break;
     }
     // The next step is staged into the other slot while this step's H-pass runs, unless
     // one of the two is the first step of a column run (which fills both slots); then it
@@ -1038,7 +1061,7 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
         const long long q = __double2ll_rn(s * kFixScale);
         atomicAdd(a.acc + cur.img, static_cast<unsigned long long>(q));
         if (l1) {
-          const long long q1 = __double2ll_rn(s1 * kFixScale);
+          const long long q1 = __double2ll_rn(s1 * kFixScaleL1);
           atomicAdd(a.acc_l1 + cur.img, static_cast<unsigned long long>(q1));
         }
       }
@@ -1051,6 +1074,7 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   if (!a.reduce) return;
   __syncthreads();
   if (threadIdx.x == 0) {
+    if (failed) atomicOr(a.ticket + 1, 1u);  // the call's "failed" word
     __threadfence();
     const unsigned prev = atomicInc(a.ticket, gridDim.x - 1);
     s_last = (prev == gridDim.x - 1) ? 1u : 0u;
@@ -1058,13 +1082,18 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  if (threadIdx.x == 0) s_last = atomicExch(a.ticket + 1, 0u) != 0u ? 2u : 1u;
+  __syncthreads();
+  // a CTA of this call gave up: every output of the call is NaN (the accumulators are
+  // still zeroed for the next call)
+  const double poison = s_last == 2u ? __longlong_as_double(0x7ff8000000000000ll) : 0.0;
   double local = 0.0, local_l1 = 0.0;
   for (int b = threadIdx.x; b < g.B; b += kThreads) {
     const long long q = static_cast<long long>(atomicExch(a.acc + b, 0ull));
-    const double s = static_cast<double>(q) * (1.0 / kFixScale);
+    const double s = static_cast<double>(q) * (1.0 / kFixScale) + poison;
     double s1 = 0.0;
     if (l1) s1 = static_cast<double>(static_cast<long long>(atomicExch(a.acc_l1 + b, 0ull))) *
-                 (1.0 / kFixScale);
+                 (1.0 / kFixScaleL1);
     if (a.image_sums) a.image_sums[b] = s;
     if (a.reduce == 2)
       a.out[b] = static_cast<float>(s * static_cast<double>(a.out_scale) +
@@ -1102,6 +1131,7 @@ struct BwdParams {
   float chain_scale;
   float l1_scale;         // fused L1 term: adds l1_scale * upstream * sign(x - y) (0: none)
   int grad_per_image, grad_dtype, aligned16, pair_ok, use_tma;
+  int wait_limit;         // polls of a step's staging wait before the step fails
 };
 
 template <int HALO, typename TIn, typename TP, bool DLMAP>
@@ -1240,16 +1270,17 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
   while (cur.n) {
     bool timed_out = false;
     if (tma) {
-      timed_out = !mbar_wait_bounded(&bar, phase);
+      timed_out = !mbar_wait_bounded(&bar, phase, a.wait_limit);
       phase ^= 1u;
     } else {
       cp_async_wait_all();
     }
     if (__syncthreads_or(timed_out)) {
       // staging did not complete: report it, give the copies in flight one more bounded
-      // wait so none lands after the CTA has exited, and leave
+      // wait so none lands after the CTA has exited, and leave (the rest of the CTA's
+      // gradient range is not written)
       if (threadIdx.x == 0) atomicOr(&g_device_error, kErrStagingTimeout);
-      mbar_wait_bounded(&bar, phase ^ 1u);
+      mbar_wait_bounded(&bar, phase ^ 1u, kWaitLimit);
       return;
     }
     // This step's epilogue operands: the image pairs of the thread's output pixels. The

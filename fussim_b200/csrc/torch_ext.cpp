@@ -475,4 +475,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     const int st = fssim_set_reserved_sms(n);
     if (st != FSSIM_OK) throw std::invalid_argument(fssim_last_error());
   });
+  // device error flag of the current CUDA device (synchronises with it)
+  m.def("poll_device_error", [](bool clear) {
+    unsigned code = 0;
+    check_status(fssim_poll_device_error(&code, clear ? 1 : 0));
+    return static_cast<int64_t>(code);
+  });
+  m.def("set_staging_wait_limit", [](int64_t polls) {
+    check_status(fssim_set_staging_wait_limit(static_cast<long long>(polls)));
+  });
+  m.def("set_gather_timeout_us", [](int64_t us) {
+    check_status(fssim_set_gather_timeout_us(static_cast<long long>(us)));
+  });
 }

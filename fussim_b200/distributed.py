@@ -12,12 +12,21 @@ values in rank order. A step then costs two kernel launches on the host, where a
 all-reduce call costs about 35 us of host time, more than the kernels of a 1080p step
 leave. Elsewhere (gloo, or more than 8 ranks) the sum is all-reduced with torch.distributed.
 
+Failure behaviour: the gather waits at most 10 s (``set_gather_timeout``) for the other
+ranks' sums; on time-out that step's value is NaN and a device
+flag is set, which ``fussim_b200.check_device_errors()`` turns into a RuntimeError. A rank
+expected to fall further behind (checkpointing, evaluation) should meet the others at a
+host-side barrier first. On the ``dist.all_reduce`` path, the process group's own timeout
+applies.
+
 The reference has no distributed path; this is the engine's data-parallel form of
 ``fused_ssim`` (fussim/__init__.py:451-580): the value equals ``fused_ssim`` of the
 concatenated global batch.
 """
 
 from __future__ import annotations
+
+import socket
 
 import torch
 import torch.distributed as dist
@@ -26,6 +35,13 @@ from . import functional as F
 
 _count_cache: dict = {}
 _mailboxes: dict = {}
+
+
+def set_gather_timeout(seconds: float) -> None:
+    """How long the peer exchange waits for the other ranks' sums before it gives up
+    (default 10 s; ``seconds <= 0`` restores it). Process-wide; applies to later steps."""
+    us = int(seconds * 1e6) if seconds > 0 else 0
+    F._ensure_cuda_extension().set_gather_timeout_us(us)
 
 
 def global_count(local_count: int, group=None) -> int:
@@ -45,6 +61,7 @@ class _Mailboxes:
 
     def __init__(self, group, device):
         ext = F._ensure_cuda_extension()
+        self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         with torch.cuda.device(device):
@@ -66,23 +83,45 @@ class _Mailboxes:
         self.ptrs = []
 
 
+def _host_identity() -> str:
+    """This machine as seen by the other ranks: host name plus the kernel's boot id, so
+    containers that share a host name on different machines are told apart."""
+    try:
+        with open("/proc/sys/kernel/random/boot_id") as f:
+            boot = f.read().strip()
+    except OSError:
+        boot = ""
+    return f"{socket.gethostname()}/{boot}"
+
+
+def _one_host(group) -> bool:
+    """True when every rank of the group runs on this machine (CUDA IPC needs that)."""
+    ids = [None] * dist.get_world_size(group)
+    dist.all_gather_object(ids, _host_identity(), group=group)
+    return len(set(ids)) == 1
+
+
 def _mailboxes_for(group, device):
     """The group's mailboxes (created on first use), or None where the peer path is not
-    available: a backend other than NCCL, or more than 8 ranks."""
+    available: a backend other than NCCL, more than 8 ranks, or ranks on several machines
+    (decided once per group, collectively, on its first sharded step)."""
     if dist.get_backend(group) != "nccl" or dist.get_world_size(group) > 8:
         return None
     key = (id(group), device.index)
     if key not in _mailboxes:
-        _mailboxes[key] = _Mailboxes(group, device)
+        _mailboxes[key] = _Mailboxes(group, device) if _one_host(group) else None
     return _mailboxes[key]
 
 
 def release_mailboxes():
-    """Unmap and free every group's mailboxes. Every rank must call it, after its last
-    sharded step and before destroy_process_group (the barrier keeps a rank from freeing
-    its mailbox while a peer may still write into it)."""
+    """Unmap and free every group's mailboxes. Every rank of each group that ran a sharded
+    step must call it, after its last sharded step and before destroy_process_group (the
+    barrier on that group keeps a rank from freeing its mailbox while a peer may still write
+    into it)."""
     for mb in list(_mailboxes.values()):
-        dist.barrier()
+        if mb is None:
+            continue
+        dist.barrier(group=mb.group)
         mb.release()
     _mailboxes.clear()
 

@@ -82,6 +82,34 @@ def check_compatibility(warn=True):
     return len(issues) == 0, issues
 
 
+_DEVICE_ERROR_BITS = {
+    1: "a kernel's input staging did not complete within its bounded wait (the reduced "
+       "outputs of that call are NaN; its per-pixel outputs are incomplete)",
+    2: "the sharded exchange gave up waiting for another rank (that step's value is NaN)",
+}
+
+
+def poll_device_error(clear: bool = True) -> int:
+    """Failures the kernels recorded on the current CUDA device since the last clear, as a
+    bit set (0 = none; the bits are those of ``check_device_errors``). Synchronises with the
+    device, so call it between steps (e.g. when a loss comes back NaN), not inside one."""
+    return int(_ensure_cuda_extension().poll_device_error(bool(clear)))
+
+
+def check_device_errors(clear: bool = True) -> None:
+    """Raise RuntimeError if a kernel recorded a failure on the current CUDA device.
+
+    The kernels never trap: a staging copy that does not arrive within its bounded wait, or
+    a sharded exchange whose peer does not answer in time, ends the affected work, writes
+    NaN to the reduced result and records a bit in a device flag. This reads (and by default
+    clears) that flag.
+    """
+    code = poll_device_error(clear)
+    if code:
+        msgs = [m for bit, m in _DEVICE_ERROR_BITS.items() if code & bit]
+        raise RuntimeError(f"fussim_b200 device error 0x{code:x}: " + "; ".join(msgs))
+
+
 def _get_halo(window_size: int) -> int:
     return (window_size - 1) // 2
 

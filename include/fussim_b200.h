@@ -61,10 +61,26 @@ const char* fssim_last_error(void);
 const char* fssim_version(void);
 
 /* Failures detected inside the kernels on the current device since the flag was last
- * cleared, as a bit set (0 = none). Bit 0: a kernel's input staging did not complete within
- * its bounded wait; that kernel left its outputs incomplete (and, for fssim_forward, its
- * workspace not zero-filled). Synchronises with the device. clear != 0 resets the flag. */
+ * cleared, as a bit set (0 = none). Synchronises with the device. clear != 0 resets the flag.
+ *  Bit 0: a kernel's input staging did not complete within its bounded wait. The CTA that
+ *         gave up stops; a forward with a reduction still completes its reduction, writes
+ *         NaN to every reduced output of that call (out, image_sums, a sharded rank's
+ *         published sum) and leaves its workspace zero-filled, so the next call on the same
+ *         workspace is unaffected. Per-pixel outputs (map, partials, gradient) of the
+ *         failed call are incomplete.
+ *  Bit 1: fssim_dp_gather gave up waiting for another rank (see section 3); it wrote NaN. */
 int fssim_poll_device_error(unsigned* code, int clear);
+
+/* Polls of a staging step's wait before the step gives up (bit 0 above). polls < 0 restores
+ * the default (2^20 polls, milliseconds). polls == 0 makes every step that is staged by the
+ * tensor memory accelerator give up at once: a way to exercise the failure path. Applies to
+ * launches made after the call; process-wide. */
+int fssim_set_staging_wait_limit(long long polls);
+
+/* How long fssim_dp_gather waits for the other ranks before it gives up (bit 1 above), in
+ * microseconds of the device's global timer. us <= 0 restores the default (10 s).
+ * Applies to launches made after the call; process-wide. */
+int fssim_set_gather_timeout_us(long long us);
 
 /* Number of SMs the kernels' persistent grids leave unused (default 0), for callers that
  * run another kernel concurrently, e.g. a collective overlapping the backward: a grid that
@@ -217,8 +233,10 @@ int fssim_forward_noalloc(const fssim_forward_args* args, fssim_stream_t stream)
  *    exports it (fssim_ipc_get_handle), exchanges the handles with the other ranks by any
  *    host channel, and maps the peers' mailboxes (fssim_ipc_open_handle).
  *    Per step: every rank calls fssim_forward_dp with the same seq (1, 2, 3, ...), then
- *    fssim_dp_gather. The gather waits for the other ranks with a bounded poll (about
- *    0.3 s); on time-out it writes NaN and sets bit 1 of fssim_poll_device_error.
+ *    fssim_dp_gather. The gather waits for the other ranks for at most the time set by
+ *    fssim_set_gather_timeout_us (default 10 s); on time-out it writes NaN and sets bit 1
+ *    of fssim_poll_device_error. A rank that falls further behind (e.g. while it writes a
+ *    checkpoint) must first bring the others to a host-side barrier.
  * ------------------------------------------------------------------------------------ */
 
 #define FSSIM_DP_MAX_RANKS 8

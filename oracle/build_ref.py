@@ -13,7 +13,7 @@ The module exposes the five reference entry points (`csrc/ext.cpp:11-17`):
 `fusedssim`, `fusedssim_backward`, `fusedssim_fp16`, `fusedssim_fp16_train`,
 `fusedssim_fp16_backward`.
 
-Usage: python oracle/build_ref.py [--reference /root/reference]
+Usage: python oracle/build_ref.py [--reference DIR]
 """
 
 from __future__ import annotations
@@ -29,13 +29,20 @@ REF_DIR = os.path.join(HERE, "_ref")
 MODULE_NAME = "fussim_ref_cuda"
 
 
+def reference_dir() -> str:
+    """Where the read-only reference checkout lies: $FUSSIM_REFERENCE_DIR, else the build
+    container's checkout location. Only the build recipes read it; nothing does at run time."""
+    return os.environ.get("FUSSIM_REFERENCE_DIR", "/root/reference")
+
+
 def built_path() -> str | None:
     """Path of the built reference extension, or None if it has not been built."""
     hits = sorted(glob.glob(os.path.join(REF_DIR, MODULE_NAME + "*.so")))
     return hits[0] if hits else None
 
 
-def build(reference: str = "/root/reference", verbose: bool = False) -> str:
+def build(reference: str | None = None, verbose: bool = False) -> str:
+    reference = reference or reference_dir()
     csrc = os.path.join(reference, "csrc")
     sources = [os.path.join(csrc, f) for f in ("ssim.cu", "ssim_fp16.cu", "ext.cpp")]
     for s in sources:
@@ -88,7 +95,8 @@ def load():
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None, help="reference checkout "
+                    "(default: $FUSSIM_REFERENCE_DIR or the container's checkout)")
     ap.add_argument("--verbose", action="store_true")
     a = ap.parse_args()
     out = build(a.reference, a.verbose)

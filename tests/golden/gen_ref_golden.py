@@ -77,7 +77,7 @@ def record(ext, shape, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--out", default=os.path.join(ROOT, "gpurun_out", "golden"))
+    ap.add_argument("--out", default=os.path.join(ROOT, "tests", "golden"))
     a = ap.parse_args()
     os.makedirs(a.out, exist_ok=True)
     ext = build_ref.load()

@@ -22,6 +22,9 @@ import types
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
 CASES = [((1, 3, 32, 32), 7), ((2, 1, 23, 37), 8), ((1, 2, 48, 53), 9)]
 
 
@@ -38,10 +41,13 @@ def load_reference_test_module(reference: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=None,
+                    help="reference checkout (default: $FUSSIM_REFERENCE_DIR or the container's)")
     ap.add_argument("--out", default=os.path.join(HERE, "ref_test_oracle.pt"))
     a = ap.parse_args()
-    mod = load_reference_test_module(a.reference)
+    from oracle import build_ref
+
+    mod = load_reference_test_module(a.reference or build_ref.reference_dir())
     out = {"source": "tests/test_ssim.py:reference_ssim", "cases": []}
     for shape, seed in CASES:
         g = torch.Generator().manual_seed(seed)
