@@ -163,6 +163,8 @@ bool encode_rows(CUtensorMap* m, const void* base, size_t esize, const fssim::Ge
   if ((static_cast<size_t>(g.W) * esize) % 16 != 0) return false;
   const int64_t planes = static_cast<int64_t>(g.B) * g.C;
   if (planes < 1 || planes > INT_MAX || g.H < 1 || g.W < 1) return false;
+  // 2-byte elements (half or bfloat16) use one map type: the copy is bitwise and its zero
+  // fill is +0 in both formats
   const bool f32 = esize == 4;
   const int w = f32 ? fssim::StagePitch<float>::value : fssim::StagePitch<__half>::value;
   // A tensor map is a pure function of (base, shape, element size, box). The driver's
@@ -519,8 +521,8 @@ int forward_impl(const fssim_forward_args* a, const fssim::DpParams* dp, cudaStr
   if (st) return st;
   st = check_shape(a->B, a->C, a->H, a->W);
   if (st) return st;
-  if (a->dtype != FSSIM_F32 && a->dtype != FSSIM_F16)
-    return fail(FSSIM_ERR_DTYPE, "img dtype must be F32 or F16");
+  if (a->dtype != FSSIM_F32 && a->dtype != FSSIM_F16 && a->dtype != FSSIM_BF16)
+    return fail(FSSIM_ERR_DTYPE, "img dtype must be F32, F16 or BF16");
   if (a->train && !(a->partial_dtype == FSSIM_F32 ||
                     (a->partial_dtype == FSSIM_F16 && a->dtype == FSSIM_F16)))
     return fail(FSSIM_ERR_DTYPE, "partials must be F32 (or F16 with F16 images)");
@@ -599,6 +601,10 @@ int forward_impl(const fssim_forward_args* a, const fssim::DpParams* dp, cudaStr
   if (a->dtype == FSSIM_F32) {
     if (a->train) return dispatch_fwd<float, float, true, true>(ws, p, s);
     return dispatch_fwd<float, float, false, true>(ws, p, s);
+  }
+  if (a->dtype == FSSIM_BF16) {
+    if (a->train) return dispatch_fwd<__nv_bfloat16, float, true, true>(ws, p, s);
+    return dispatch_fwd<__nv_bfloat16, float, false, true>(ws, p, s);
   }
   if (!a->train) return dispatch_fwd<__half, float, false, true>(ws, p, s);
   if (a->partial_dtype == FSSIM_F16) return dispatch_fwd<__half, __half, true, true>(ws, p, s);
@@ -730,8 +736,8 @@ int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
   if (st) return st;
   st = check_shape(a->B, a->C, a->H, a->W);
   if (st) return st;
-  if (a->dtype != FSSIM_F32 && a->dtype != FSSIM_F16)
-    return fail(FSSIM_ERR_DTYPE, "img dtype must be F32 or F16");
+  if (a->dtype != FSSIM_F32 && a->dtype != FSSIM_F16 && a->dtype != FSSIM_BF16)
+    return fail(FSSIM_ERR_DTYPE, "img dtype must be F32, F16 or BF16");
   if (!(a->partial_dtype == FSSIM_F32 || (a->partial_dtype == FSSIM_F16 && a->dtype == FSSIM_F16)))
     return fail(FSSIM_ERR_DTYPE, "partials must be F32 (or F16 with F16 images)");
   if (a->grad_dtype < FSSIM_F32 || a->grad_dtype > FSSIM_BF16)
@@ -766,6 +772,7 @@ int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
   const int ws = a->window_size;
   cudaStream_t s = stream;
   if (a->dtype == FSSIM_F32) return dispatch_bwd<float, float, false>(ws, p, s);
+  if (a->dtype == FSSIM_BF16) return dispatch_bwd<__nv_bfloat16, float, false>(ws, p, s);
   if (a->partial_dtype == FSSIM_F16) return dispatch_bwd<__half, __half, false>(ws, p, s);
   return dispatch_bwd<__half, float, false>(ws, p, s);
 }

@@ -60,6 +60,13 @@ constexpr double kFixScaleL1 = 1048576.0;    // 2^20: L1 sums
 template <typename T> struct StagePitch;
 template <> struct StagePitch<float> { static constexpr int value = 84; };   // 84 words
 template <> struct StagePitch<__half> { static constexpr int value = 88; };  // 44 words
+template <> struct StagePitch<__nv_bfloat16> { static constexpr int value = 88; };
+
+// Inputs read as IEEE half use the reference's half-rounded Gaussian taps (its FP16 kernels
+// do); FP32 and bfloat16 inputs use the FP32 taps. bfloat16 has no reference kernel: it is
+// this engine's native path for bfloat16 images, FP32 arithmetic on the widened values.
+template <typename T> struct HalfTaps { static constexpr bool value = false; };
+template <> struct HalfTaps<__half> { static constexpr bool value = true; };
 
 // Moment-ring pitch in floats: NMAP rows of 64 plus 2. The H-pass stores 8-byte column
 // pairs from 16 consecutive rows per half warp; a pitch of 2 mod 32 words puts each half
@@ -244,6 +251,12 @@ __device__ __forceinline__ void grid_launch_dependents() {
 
 __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float2 to_f2(__half2 v) { return __half22float2(v); }
+__device__ __forceinline__ float2 to_f2(__nv_bfloat162 v) { return __bfloat1622float2(v); }
+template <typename T> struct Pair2;
+template <> struct Pair2<__half> { using type = __half2; };
+template <> struct Pair2<__nv_bfloat16> { using type = __nv_bfloat162; };
 
 // Load NV consecutive staged elements (16-byte aligned) as floats.
 template <int NV>
@@ -257,15 +270,17 @@ __device__ __forceinline__ void load_vec(const float* p, float (&v)[NV]) {
     v[4 * q + 3] = t.w;
   }
 }
-template <int NV>
-__device__ __forceinline__ void load_vec(const __half* p, float (&v)[NV]) {
+template <int NV, typename T2>
+__device__ __forceinline__ void load_vec(const T2* p, float (&v)[NV]) {
+  static_assert(sizeof(T2) == 2, "2-byte elements");
+  using P2 = typename Pair2<T2>::type;
 #pragma unroll
   for (int q = 0; q < NV / 8; ++q) {
     const uint4 t = reinterpret_cast<const uint4*>(p)[q];
-    const __half2* h = reinterpret_cast<const __half2*>(&t);
+    const P2* h = reinterpret_cast<const P2*>(&t);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float2 f = __half22float2(h[e]);
+      const float2 f = to_f2(h[e]);
       v[8 * q + 2 * e] = f.x;
       v[8 * q + 2 * e + 1] = f.y;
     }
@@ -344,7 +359,8 @@ __device__ __forceinline__ float2 load2(const T* base, I idx, bool pair, bool in
     if constexpr (sizeof(T) == 4) {
       return __ldg(reinterpret_cast<const float2*>(base + idx));
     } else {
-      return __half22float2(__ldg(reinterpret_cast<const __half2*>(base + idx)));
+      using P2 = typename Pair2<T>::type;
+      return to_f2(__ldg(reinterpret_cast<const P2*>(base + idx)));
     }
   }
   return make_float2(in0 ? to_f(base[idx]) : 0.f, in1 ? to_f(base[idx + 1]) : 0.f);
@@ -730,7 +746,7 @@ struct FwdParams {
 // (MERGED = false) so their per-pixel outputs follow its arithmetic order exactly.
 template <int HALO, typename TIn, typename TP, bool TRAIN, bool MERGED>
 struct FwdConfig {
-  static constexpr bool kHalfW = sizeof(TIn) == 2;
+  static constexpr bool kHalfW = HalfTaps<TIn>::value;
   static constexpr int kMaps = MERGED ? 4 : 5;
   static constexpr int kMaxR = MaxRows<HALO>::value;
   static constexpr int kSRows = StageRows<HALO>::value;
@@ -756,7 +772,7 @@ struct FwdConfig {
 // exactly one task of one step).
 template <int HALO, typename TIn, int MAXR, bool MERGED>
 __device__ __forceinline__ void fwd_hpass(const TIn* sx, const TIn* sy, float* ring, int nh,
-                                          int hdst, const Taps2<HALO, sizeof(TIn) == 2>& T,
+                                          int hdst, const Taps2<HALO, HalfTaps<TIn>::value>& T,
                                           bool l1, int l1_i0, int l1_i1, int l1_cols,
                                           float& l1_sum) {
   constexpr int SP = StagePitch<TIn>::value;
@@ -1136,7 +1152,7 @@ struct BwdParams {
 
 template <int HALO, typename TIn, typename TP, bool DLMAP>
 struct BwdConfig {
-  static constexpr bool kHalfW = sizeof(TIn) == 2;
+  static constexpr bool kHalfW = HalfTaps<TIn>::value;
   static constexpr int kMaxR = MaxRows<HALO>::value;
   static constexpr int kSRows = StageRows<HALO>::value;
   // a first step's boxes fit the staging rows; a regular step's boxes fit one slot
@@ -1160,7 +1176,7 @@ struct BwdConfig {
 // general path, as the reference multiplies at load, csrc/ssim.cu:408-411).
 template <int HALO, typename TIn, typename TP, bool DLMAP, int MAXR>
 __device__ __forceinline__ void bwd_hpass(const TP* sp, const float* sdl, float* ring, int nh,
-                                          int hdst, const Taps2<HALO, sizeof(TIn) == 2>& T) {
+                                          int hdst, const Taps2<HALO, HalfTaps<TIn>::value>& T) {
   constexpr int SP = StagePitch<TP>::value;
   constexpr int RP = RingPitch<3>::value;
   constexpr int HA = (sizeof(TP) == 2 || HALO > 4) ? 8 : 4;

@@ -213,7 +213,9 @@ std::tuple<torch::Tensor, torch::Tensor, torch::Tensor> loss_forward_impl(
   auto b = img2.contiguous();
   TORCH_CHECK(a.scalar_type() == b.scalar_type(), "img1 and img2 must have the same dtype");
   const int dt = dtype_code(a.scalar_type());
-  TORCH_CHECK(dt == FSSIM_F32 || dt == FSSIM_F16, "images must be float32 or float16");
+  TORCH_CHECK(dt == FSSIM_F32 || dt == FSSIM_F16 || dt == FSSIM_BF16,
+              "images must be float32, float16 or bfloat16");
+  TORCH_CHECK(!(half_partials && dt == FSSIM_BF16), "FP16 partials need float16 images");
   const int64_t B = a.size(0);
   const int pdt = (half_partials && dt == FSSIM_F16) ? FSSIM_F16 : FSSIM_F32;
   auto partials =

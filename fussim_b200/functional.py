@@ -228,12 +228,16 @@ def _reduce(img1, img2, C1, C2, window_size, valid, clamp, reduce, train, half):
 
 
 def _float_path_inputs(img1, img2):
-    # Outside autocast the reference's FP32 kernels take float32 tensors; half tensors are
-    # read natively by the FP16-input kernels here, bfloat16 is widened to float32.
-    if img1.dtype == torch.bfloat16:
-        img1 = img1.float()
-    if img2.dtype == torch.bfloat16:
-        img2 = img2.float()
+    # Outside autocast the reference's FP32 kernels take float32 tensors. Here half tensors
+    # are read natively by the FP16-input kernels, a bfloat16 pair by the bfloat16-input
+    # kernels (FP32 arithmetic and FP32 taps on the widened values: the same result as the
+    # float32 path on img.float()), and a bfloat16 image paired with another dtype is
+    # widened to float32.
+    if (img1.dtype == torch.bfloat16) != (img2.dtype == torch.bfloat16):
+        if img1.dtype == torch.bfloat16:
+            img1 = img1.float()
+        if img2.dtype == torch.bfloat16:
+            img2 = img2.float()
     return img1, img2
 
 
