@@ -480,18 +480,23 @@ def measure_fp16(fb, synthetic, pairs, dev, K, warm, step_ms_fp32):
         return event_time(st, iters, prime_us=3000)
 
     n1080 = pairs[0][0].numel()
-    t16_1080 = run(pairs, "same", True)
-    res = {"1080p_same": {"workload": "1x3x1080x1920, padding same, train, fwd+bwd",
+    # FP16 images (the FP16 workload's own dtype): no cast kernel in the step
+    p16 = [(x.detach().half().requires_grad_(True), y.half()) for x, y in pairs]
+    t16_1080 = run(p16, "same", True)
+    del p16
+    res = {"1080p_same": {"workload": "1x3x1080x1920, padding same, train, fwd+bwd; FP32 "
+                                       "images vs the same images in FP16 under autocast",
                           "fp32_ms": step_ms_fp32, "fp16_ms": t16_1080,
                           "fp32_value": n1080 / (step_ms_fp32 * 1e-3) / 1e6,
                           "fp16_value": n1080 / (t16_1080 * 1e-3) / 1e6,
                           "fp16_over_fp32": step_ms_fp32 / t16_1080}}
-    # 8x3x1024^2 blob pairs, valid padding: FP32 inputs for both legs (autocast rounds them
-    # to FP16 inside the FP16 leg, as the reference does)
+    # 8x3x1024^2 blob pairs, valid padding: the same values as FP32 images (FP32 leg) and as
+    # FP16 images under autocast (FP16 leg, the workload's own form)
     h = [synthetic.make_pair("fp16_1024_valid", seed=77 + k) for k in range(2)]
     p = [(a.float().to(dev).requires_grad_(True), b.float().to(dev)) for a, b in h]
     n = p[0][0].numel()
     t32 = run(p, "valid", False)
+    p = [(a.to(dev).requires_grad_(True), b.to(dev)) for a, b in h]
     t16 = run(p, "valid", True)
     res["8x1024_valid"] = {"workload": "8x3x1024x1024 blob pairs, padding valid, train, fwd+bwd",
                            "fp32_ms": t32, "fp16_ms": t16,

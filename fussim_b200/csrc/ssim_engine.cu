@@ -9,12 +9,14 @@
 #include <climits>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "fussim_b200.h"
 #include "ssim_kernels.cuh"
+#include "ssim_stream.cuh"
 
 namespace {
 
@@ -96,7 +98,8 @@ int device_sms(int* sms) {
 // number of resident CTAs per SM. `cache` is owned by one kernel instantiation (it lives in
 // the launch_* template below), so every instantiation gets its own per-device entry.
 template <typename Kernel>
-int kernel_occupancy(Kernel k, size_t smem, int (&cache)[64], std::mutex& mu, int* occ) {
+int kernel_occupancy(Kernel k, size_t smem, int (&cache)[64], std::mutex& mu, int* occ,
+                     int threads = fssim::kThreads) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
@@ -107,7 +110,7 @@ int kernel_occupancy(Kernel k, size_t smem, int (&cache)[64], std::mutex& mu, in
     if (e != cudaSuccess)
       return fail(FSSIM_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     int v = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k, fssim::kThreads, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k, threads, smem);
     if (e != cudaSuccess || v <= 0)
       return fail(FSSIM_ERR_CUDA, std::string("occupancy query failed: ") + cudaGetErrorString(e));
     cache[dev] = v;
@@ -157,7 +160,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 // FP32 or FP16 elements, boxes of kBoxRows rows x one staged row pitch of columns,
 // zero fill outside. False (the kernels then stage with cp.async) when the layout does not
 // meet the copy unit's rules: 16-byte aligned base, row pitch a multiple of 16 bytes.
-bool encode_rows(CUtensorMap* m, const void* base, size_t esize, const fssim::Geometry& g) {
+bool encode_rows(CUtensorMap* m, const void* base, size_t esize, const fssim::Geometry& g,
+                 int box_rows) {
   const PFN_cuTensorMapEncodeTiled_v12000 fn = tensor_map_encoder();
   if (!fn || !base || !aligned(base, 16)) return false;
   if ((static_cast<size_t>(g.W) * esize) % 16 != 0) return false;
@@ -174,16 +178,16 @@ bool encode_rows(CUtensorMap* m, const void* base, size_t esize, const fssim::Ge
     const void* base;
     int64_t W, H, planes;
     size_t esize;
-    int box_w;
+    int box_w, box_h;
     bool valid;
     CUtensorMap map;
   };
   static thread_local Entry cache[32];
   const uintptr_t key = reinterpret_cast<uintptr_t>(base);
   Entry& e = cache[((key >> 8) ^ (key >> 20) ^ static_cast<uintptr_t>(g.W) ^
-                    static_cast<uintptr_t>(w) * 7u) % 32];
+                    static_cast<uintptr_t>(w) * 7u ^ static_cast<uintptr_t>(box_rows) * 13u) % 32];
   if (e.valid && e.base == base && e.W == g.W && e.H == g.H && e.planes == planes &&
-      e.esize == esize && e.box_w == w) {
+      e.esize == esize && e.box_w == w && e.box_h == box_rows) {
     *m = e.map;
     return true;
   }
@@ -191,7 +195,7 @@ bool encode_rows(CUtensorMap* m, const void* base, size_t esize, const fssim::Ge
                         static_cast<cuuint64_t>(planes)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(g.W) * esize,
                            static_cast<cuuint64_t>(g.HW) * esize};
-  cuuint32_t box[3] = {static_cast<cuuint32_t>(w), static_cast<cuuint32_t>(fssim::kBoxRows), 1u};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(w), static_cast<cuuint32_t>(box_rows), 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   const CUresult r =
       fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
@@ -205,21 +209,23 @@ bool encode_rows(CUtensorMap* m, const void* base, size_t esize, const fssim::Ge
   e.planes = planes;
   e.esize = esize;
   e.box_w = w;
+  e.box_h = box_rows;
   e.map = *m;
   e.valid = true;
   return true;
 }
 
-// Sets p.use_tma when every staged tensor of the forward has a tensor map.
-void set_fwd_tma(fssim::FwdParams& p, size_t esize) {
-  p.use_tma = encode_rows(&p.tmap[0], p.img1, esize, p.g) &&
-              encode_rows(&p.tmap[1], p.img2, esize, p.g);
+// Sets p.use_tma when every staged tensor of the forward has a tensor map (boxes of
+// box_rows rows: kBoxRows for the tile kernels, kSStep for the streaming kernels).
+void set_fwd_tma(fssim::FwdParams& p, size_t esize, int box_rows = fssim::kBoxRows) {
+  p.use_tma = encode_rows(&p.tmap[0], p.img1, esize, p.g, box_rows) &&
+              encode_rows(&p.tmap[1], p.img2, esize, p.g, box_rows);
 }
-void set_bwd_tma(fssim::BwdParams& p, size_t pesize) {
-  bool ok = encode_rows(&p.tmap[0], p.p0, pesize, p.g) &&
-            encode_rows(&p.tmap[1], p.p1, pesize, p.g) &&
-            encode_rows(&p.tmap[2], p.p2, pesize, p.g);
-  if (ok && p.dl) ok = encode_rows(&p.tmap[3], p.dl, sizeof(float), p.g);
+void set_bwd_tma(fssim::BwdParams& p, size_t pesize, int box_rows = fssim::kBoxRows) {
+  bool ok = encode_rows(&p.tmap[0], p.p0, pesize, p.g, box_rows) &&
+            encode_rows(&p.tmap[1], p.p1, pesize, p.g, box_rows) &&
+            encode_rows(&p.tmap[2], p.p2, pesize, p.g, box_rows);
+  if (ok && p.dl) ok = encode_rows(&p.tmap[3], p.dl, sizeof(float), p.g, box_rows);
   p.use_tma = ok;
 }
 
@@ -227,10 +233,11 @@ void set_bwd_tma(fssim::BwdParams& p, size_t pesize) {
 // previous kernel on the stream finishes; it waits (griddepcontrol.wait) before touching
 // global memory.
 template <typename Kernel, typename Params>
-cudaError_t launch_pdl(Kernel k, int grid, size_t smem, cudaStream_t stream, const Params& p) {
+cudaError_t launch_pdl(Kernel k, int grid, size_t smem, cudaStream_t stream, const Params& p,
+                       int threads = fssim::kThreads) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(fssim::kThreads);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -291,6 +298,95 @@ int launch_bwd(const fssim::BwdParams& p, cudaStream_t stream) {
     return fail(FSSIM_ERR_CUDA, std::string("ssim backward launch: ") + cudaGetErrorString(e));
   }
   return launch_error("ssim backward launch");
+}
+
+// The fused loss path's column-streaming kernels (ssim_stream.cuh).
+template <int HALO, typename TIn, typename TP, bool TRAIN>
+int launch_sfwd(const fssim::FwdParams& p, cudaStream_t stream) {
+  using Cfg = fssim::SFwdConfig<HALO, TIn, TP, TRAIN>;
+  auto k = fssim::loss_fwd_kernel<HALO, TIn, TP, TRAIN>;
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int occ = 0, sms = 0;
+  int st = kernel_occupancy(k, Cfg::kSmem, cache, mu, &occ, fssim::kSThreads);
+  if (st) return st;
+  st = device_sms(&sms);
+  if (st) return st;
+  const int grid = grid_size(p.g, occ, sms);
+  if ((p.g.LT + grid - 1) / grid + 2 * p.g.H > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
+  fssim::FwdParams q = p;
+  q.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
+  const cudaError_t e = launch_pdl(k, grid, Cfg::kSmem, stream, q, fssim::kSThreads);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return fail(FSSIM_ERR_CUDA, std::string("ssim loss forward launch: ") + cudaGetErrorString(e));
+  }
+  return launch_error("ssim loss forward launch");
+}
+
+template <int HALO, typename TIn, typename TP>
+int launch_sbwd(const fssim::BwdParams& p, cudaStream_t stream) {
+  using Cfg = fssim::SBwdConfig<HALO, TIn, TP>;
+  auto k = fssim::loss_bwd_kernel<HALO, TIn, TP>;
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int occ = 0, sms = 0;
+  int st = kernel_occupancy(k, Cfg::kSmem, cache, mu, &occ, fssim::kSThreads);
+  if (st) return st;
+  st = device_sms(&sms);
+  if (st) return st;
+  const int grid = grid_size(p.g, occ, sms);
+  if ((p.g.LT + grid - 1) / grid + 2 * p.g.H > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
+  fssim::BwdParams q = p;
+  q.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
+  const cudaError_t e = launch_pdl(k, grid, Cfg::kSmem, stream, q, fssim::kSThreads);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return fail(FSSIM_ERR_CUDA, std::string("ssim loss backward launch: ") + cudaGetErrorString(e));
+  }
+  return launch_error("ssim loss backward launch");
+}
+
+// Kernel family of the fused loss path (fssim_set_loss_kernels): the column-streaming
+// kernels (FSSIM_KERNELS_STREAM, default) or the 4-row tile kernels that the map entry
+// points use (FSSIM_KERNELS_TILE).
+std::atomic<int> g_loss_kernels{FSSIM_KERNELS_STREAM};
+bool loss_streaming() { return g_loss_kernels.load(std::memory_order_relaxed) == FSSIM_KERNELS_STREAM; }
+
+template <typename TIn, typename TP, bool TRAIN>
+int dispatch_loss_fwd(int ws, const fssim::FwdParams& p, cudaStream_t s, bool streaming) {
+  if (!streaming) {
+    switch (ws) {
+      case 7: return launch_fwd<3, TIn, TP, TRAIN, true>(p, s);
+      case 9: return launch_fwd<4, TIn, TP, TRAIN, true>(p, s);
+      case 11: return launch_fwd<5, TIn, TP, TRAIN, true>(p, s);
+      default: return fail(FSSIM_ERR_WINDOW, window_message(ws));
+    }
+  }
+  switch (ws) {
+    case 7: return launch_sfwd<3, TIn, TP, TRAIN>(p, s);
+    case 9: return launch_sfwd<4, TIn, TP, TRAIN>(p, s);
+    case 11: return launch_sfwd<5, TIn, TP, TRAIN>(p, s);
+    default: return fail(FSSIM_ERR_WINDOW, window_message(ws));
+  }
+}
+
+template <typename TIn, typename TP>
+int dispatch_loss_bwd(int ws, const fssim::BwdParams& p, cudaStream_t s, bool streaming) {
+  if (!streaming) {
+    switch (ws) {
+      case 7: return launch_bwd<3, TIn, TP, false>(p, s);
+      case 9: return launch_bwd<4, TIn, TP, false>(p, s);
+      case 11: return launch_bwd<5, TIn, TP, false>(p, s);
+      default: return fail(FSSIM_ERR_WINDOW, window_message(ws));
+    }
+  }
+  switch (ws) {
+    case 7: return launch_sbwd<3, TIn, TP>(p, s);
+    case 9: return launch_sbwd<4, TIn, TP>(p, s);
+    case 11: return launch_sbwd<5, TIn, TP>(p, s);
+    default: return fail(FSSIM_ERR_WINDOW, window_message(ws));
+  }
 }
 
 // MERGED selects the fused loss path's 4-map forward; the map-producing reference entry
@@ -418,6 +514,14 @@ int fssim_set_reserved_sms(int n) {
   g_last_error.clear();
   if (n < 0) return fail(FSSIM_ERR_ARGUMENT, "reserved SM count must be >= 0");
   g_reserved_sms.store(n, std::memory_order_relaxed);
+  return FSSIM_OK;
+}
+
+int fssim_set_loss_kernels(int family) {
+  g_last_error.clear();
+  if (family != FSSIM_KERNELS_STREAM && family != FSSIM_KERNELS_TILE)
+    return fail(FSSIM_ERR_ARGUMENT, "family must be FSSIM_KERNELS_STREAM or FSSIM_KERNELS_TILE");
+  g_loss_kernels.store(family, std::memory_order_relaxed);
   return FSSIM_OK;
 }
 
@@ -593,22 +697,24 @@ int forward_impl(const fssim_forward_args* a, const fssim::DpParams* dp, cudaStr
   bool pair = (a->W % 2 == 0) && (!a->ssim_map || aligned(a->ssim_map, 8));
   if (a->train) pair = pair && aligned(p.p0, 2 * PE) && aligned(p.p1, 2 * PE) && aligned(p.p2, 2 * PE);
   p.pair_ok = pair;
-  set_fwd_tma(p, E);
+  // the family is read once: its tensor maps' box height must match the kernels launched
+  const bool streaming = loss_streaming();
+  set_fwd_tma(p, E, streaming ? fssim::kSStep : fssim::kBoxRows);
   if (dp) p.dp = *dp;
 
   const int ws = a->window_size;
   cudaStream_t s = stream;
   if (a->dtype == FSSIM_F32) {
-    if (a->train) return dispatch_fwd<float, float, true, true>(ws, p, s);
-    return dispatch_fwd<float, float, false, true>(ws, p, s);
+    if (a->train) return dispatch_loss_fwd<float, float, true>(ws, p, s, streaming);
+    return dispatch_loss_fwd<float, float, false>(ws, p, s, streaming);
   }
   if (a->dtype == FSSIM_BF16) {
-    if (a->train) return dispatch_fwd<__nv_bfloat16, float, true, true>(ws, p, s);
-    return dispatch_fwd<__nv_bfloat16, float, false, true>(ws, p, s);
+    if (a->train) return dispatch_loss_fwd<__nv_bfloat16, float, true>(ws, p, s, streaming);
+    return dispatch_loss_fwd<__nv_bfloat16, float, false>(ws, p, s, streaming);
   }
-  if (!a->train) return dispatch_fwd<__half, float, false, true>(ws, p, s);
-  if (a->partial_dtype == FSSIM_F16) return dispatch_fwd<__half, __half, true, true>(ws, p, s);
-  return dispatch_fwd<__half, float, true, true>(ws, p, s);
+  if (!a->train) return dispatch_loss_fwd<__half, float, false>(ws, p, s, streaming);
+  if (a->partial_dtype == FSSIM_F16) return dispatch_loss_fwd<__half, __half, true>(ws, p, s, streaming);
+  return dispatch_loss_fwd<__half, float, true>(ws, p, s, streaming);
 }
 
 int check_dp(const fssim_dp_args* d, fssim::DpParams* out) {
@@ -768,13 +874,14 @@ int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
                 aligned(p.p1, 16) && aligned(p.p2, 16);
   p.pair_ok = (a->W % 2 == 0) && aligned(a->img1, 2 * E) && aligned(a->img2, 2 * E) &&
               aligned(a->grad, 2 * GE);
-  set_bwd_tma(p, PE);
+  const bool streaming = loss_streaming();
+  set_bwd_tma(p, PE, streaming ? fssim::kSStep : fssim::kBoxRows);
   const int ws = a->window_size;
   cudaStream_t s = stream;
-  if (a->dtype == FSSIM_F32) return dispatch_bwd<float, float, false>(ws, p, s);
-  if (a->dtype == FSSIM_BF16) return dispatch_bwd<__nv_bfloat16, float, false>(ws, p, s);
-  if (a->partial_dtype == FSSIM_F16) return dispatch_bwd<__half, __half, false>(ws, p, s);
-  return dispatch_bwd<__half, float, false>(ws, p, s);
+  if (a->dtype == FSSIM_F32) return dispatch_loss_bwd<float, float>(ws, p, s, streaming);
+  if (a->dtype == FSSIM_BF16) return dispatch_loss_bwd<__nv_bfloat16, float>(ws, p, s, streaming);
+  if (a->partial_dtype == FSSIM_F16) return dispatch_loss_bwd<__half, __half>(ws, p, s, streaming);
+  return dispatch_loss_bwd<__half, float>(ws, p, s, streaming);
 }
 
 }  // extern "C"

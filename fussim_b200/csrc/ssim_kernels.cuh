@@ -470,8 +470,9 @@ __device__ __forceinline__ Step<HALO> next_step(const Step<HALO>& c, const Geome
 }
 
 // Stage moment rows [h0, h0+nh) x columns [x0-8, x0+72) of NMAP planes into smem
-// (layout [NMAP][MAXR][PITCH]); out-of-image elements become zero.
-template <typename T, int NMAP, int MAXR, typename StepT>
+// (layout [NMAP][MAXR][PITCH]) with the NT threads of the CTA; out-of-image elements
+// become zero.
+template <typename T, int NMAP, int MAXR, typename StepT, int NT = kThreads>
 __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const Geometry& g,
                                       const StepT& s, bool aligned16) {
   constexpr int P = StagePitch<T>::value;
@@ -487,7 +488,7 @@ __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const 
     for (int m = 0; m < NMAP; ++m) {
       const T* plane = src[m] + static_cast<int64_t>(s.plane) * g.HW;
       T* dst = sm + m * MAXR * P;
-      for (int i = threadIdx.x; i < total; i += kThreads) {
+      for (int i = threadIdx.x; i < total; i += NT) {
         const int row = i / CH;
         const int ch = i - row * CH;
         const int gy = h0 + row;
@@ -504,7 +505,7 @@ __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const 
     for (int m = 0; m < NMAP; ++m) {
       const T* plane = src[m] + static_cast<int64_t>(s.plane) * g.HW;
       T* dst = sm + m * MAXR * P;
-      for (int i = threadIdx.x; i < total; i += kThreads) {
+      for (int i = threadIdx.x; i < total; i += NT) {
         const int row = i / kInCols;
         const int c = i - row * kInCols;
         const int gy = h0 + row;
@@ -522,7 +523,7 @@ __device__ __forceinline__ void stage(T* sm, const T* const (&src)[NMAP], const 
     for (int m = 0; m < NMAP; ++m) {
       const T* plane = src[m] + static_cast<int64_t>(s.plane) * g.HW;
       T* dst = sm + m * MAXR * P;
-      for (int i = threadIdx.x; i < total; i += kThreads) {
+      for (int i = threadIdx.x; i < total; i += NT) {
         const int row = i / kInCols;
         const int c = i - row * kInCols;
         const int gy = h0 + row;

@@ -1,0 +1,839 @@
+// Fused-loss kernels with a column-streaming vertical pass (sm_100a).
+//
+// These are the kernels of the fused loss path (fssim_forward / fssim_backward): the
+// forward writes the three SSIM partials and the deterministic reductions, the backward
+// applies the transposed Gaussian to the partials. They share the work decomposition of
+// the map kernels in ssim_kernels.cuh (64-column strips of the batch's planes, column runs
+// of H output rows split over a persistent grid in equal amounts of work, TMA staging one
+// step ahead), but the vertical pass is organised differently:
+//
+//   * one output column per thread: a CTA of 64 threads (2 warps) covers one strip;
+//   * the horizontal pass of a step (16 rows) writes its moment rows to a shared buffer
+//     that holds only that step's rows;
+//   * each thread keeps the last 2*HALO moment rows of its column in registers from one
+//     step to the next (a sliding window), and reads each moment value from shared memory
+//     exactly once; the vertical halo is never stored, copied or recomputed within a run
+//     part;
+//   * the first step of every run part ("preload") runs only the horizontal pass over the
+//     2*HALO rows above the part's first output row, to fill the window.
+//
+// Per output pixel this reads 16 bytes of moments from shared memory in the forward (4
+// maps) where a 4-row register tile reads 56, and it needs no halo-row copy between steps.
+// Arithmetic is the map kernels' (and the reference's) tap for tap: the horizontal pass is
+// the same code, and the vertical sum adds symmetric pairs (d = 1..HALO) then the centre,
+// so per-pixel results are bitwise identical to the map kernels'; two maps are carried per
+// packed FP32 pair ((mu_x, mu_y) and (E[x^2 + y^2], E[xy]) in the forward), which keeps the
+// packed instructions without pairing adjacent columns.
+#pragma once
+
+#include "ssim_kernels.cuh"
+
+namespace fssim {
+
+constexpr int kSThreads = 64;                 // one thread per strip column
+constexpr int kSWarps = kSThreads / 32;
+constexpr int kSStep = 8;                     // output rows per step (and rows per TMA box)
+static_assert(kSThreads == kStrip, "one output column per thread");
+
+// Horizontal pass task mapping over a 64-column strip for 2 warps: rows in groups of 8
+// (lane % 8) and chunks of 8 columns j = lane / 8 + 4 * warp, one task per thread per
+// group. The 8 lanes of a quarter warp read the same chunk of 8 consecutive staged rows.
+__device__ __forceinline__ int htask_row(int lane) { return lane & 7; }
+__device__ __forceinline__ int htask_chunk(int warp, int lane) { return (lane >> 3) + 4 * warp; }
+
+// Deterministic sum over the CTA of one double per thread (fixed shuffle tree, warps in
+// order). red holds NW doubles.
+template <int NW>
+__device__ __forceinline__ double block_sum_w(double v, double* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double s = red[0];
+#pragma unroll
+  for (int w = 1; w < NW; ++w) s += red[w];
+  return s;
+}
+
+// One step of a streaming kernel: the first step of a run part preloads the window (moment
+// rows [t - HALO, t + HALO), no outputs); a regular step produces output rows [t, t + n)
+// from the new moment rows [t + HALO, t + HALO + n). Staging: a regular step's rows fill one
+// of two slots of kSStep rows, a preload's 2*HALO rows both slots.
+template <int HALO>
+struct SStep {
+  int plane, img, chan, strip;
+  int t;      // first output row of the step (of the part, for a preload)
+  int n;      // output rows of the regular step (1..kSStep)
+  int ps;     // first output row of the part
+  int t_end;  // end row of the CTA's part of this column run
+  int rest;   // strip-rows of the CTA's range after that part
+  int slot;   // first staging row (0 or kSStep)
+  bool pre;   // preload step
+  bool live;  // false: no step
+  __device__ __forceinline__ int h0() const { return pre ? t - HALO : t + HALO; }
+  __device__ __forceinline__ int nh() const { return pre ? 2 * HALO : n; }
+  __device__ __forceinline__ bool last() const { return !pre && t + n == t_end; }
+};
+
+template <int HALO>
+__device__ __forceinline__ SStep<HALO> sfirst_step(int64_t beg, int64_t end, const Geometry& g) {
+  SStep<HALO> s;
+  const int64_t len = end - beg;
+  s.live = len > 0;
+  if (!s.live) return s;
+  const int64_t col = beg / g.H;
+  s.t = static_cast<int>(beg - col * g.H);
+  const int64_t plane = col / g.S;
+  s.plane = static_cast<int>(plane);
+  s.strip = static_cast<int>(col - plane * g.S);
+  s.img = s.plane / g.C;
+  s.chan = s.plane - s.img * g.C;
+  const int64_t seg = (g.H - s.t) < len ? (g.H - s.t) : len;
+  s.ps = s.t;
+  s.t_end = s.t + static_cast<int>(seg);
+  s.rest = static_cast<int>(len - seg);
+  s.slot = 0;
+  s.pre = true;
+  s.n = static_cast<int>(seg) < kSStep ? static_cast<int>(seg) : kSStep;
+  return s;
+}
+
+// The step after c. Its staging slot: 0 after a preload and for a preload (which are staged
+// once the previous step's horizontal pass is done), else the slot c does not use.
+template <int HALO>
+__device__ __forceinline__ SStep<HALO> snext_step(const SStep<HALO>& c, const Geometry& g) {
+  SStep<HALO> s = c;
+  if (c.pre) {  // the part's first regular step, at the same rows
+    s.pre = false;
+    s.slot = 0;
+    return s;
+  }
+  s.slot = c.slot ^ kSStep;
+  s.t = c.t + c.n;
+  if (s.t == c.t_end) {  // the CTA's part of this column run is done
+    if (c.rest == 0) {
+      s.live = false;
+      return s;
+    }
+    s.t = 0;
+    s.ps = 0;
+    s.pre = true;
+    s.slot = 0;
+    if (++s.strip == g.S) {
+      s.strip = 0;
+      ++s.plane;
+      if (++s.chan == g.C) {
+        s.chan = 0;
+        ++s.img;
+      }
+    }
+    const int H = static_cast<int>(g.H);
+    const int seg = c.rest < H ? c.rest : H;
+    s.t_end = seg;
+    s.rest = c.rest - seg;
+  }
+  const int r = s.t_end - s.t;
+  s.n = r < kSStep ? r : kSStep;
+  return s;
+}
+
+// Start of CTA b's range of strip-rows for the streaming kernels: as cta_range_start, with a
+// run part costing its rows plus the 2*HALO rows of its preload.
+template <int HALO>
+__device__ __forceinline__ int64_t scta_range_start(const Geometry& g, int64_t b, int64_t G) {
+  const int64_t runs = g.LT / g.H;
+  const int64_t per = g.H + 2 * HALO;
+  const int64_t A = (runs * per * b) / G;
+  const int64_t r = A / per;
+  const int64_t o = A - r * per;
+  if (o >= g.H) return (r + 1) * g.H;
+  return r * g.H + (o / kSStep) * kSStep;
+}
+
+// Bytes the TMA staging of nh rows delivers for NMAP maps of element type T (boxes of
+// kSStep rows).
+template <typename T, int NMAP>
+__device__ __forceinline__ unsigned sstep_bytes(int nh) {
+  const int nbox = (nh + kSStep - 1) / kSStep;
+  return static_cast<unsigned>(NMAP * nbox * kSStep * StagePitch<T>::value * sizeof(T));
+}
+
+// TMA staging of step st by the lanes of warp 0: lane m * nbox + b copies box b (kSStep rows)
+// of map m into rows [slot + b * kSStep, ...) of the layout [NMAP][2 * kSStep][pitch].
+template <typename T, int NMAP, int HALO>
+__device__ __forceinline__ void sstage_tma(T* stg, const CUtensorMap* maps, const SStep<HALO>& st,
+                                           uint64_t* bar) {
+  constexpr int P = StagePitch<T>::value;
+  constexpr int SROWS = 2 * kSStep;
+  const int lane = threadIdx.x & 31;
+  const int nbox = (st.nh() + kSStep - 1) / kSStep;
+  if (lane == 0) mbar_arrive_expect_tx(bar, sstep_bytes<T, NMAP>(st.nh()));
+  if (lane < NMAP * nbox) {
+    const int m = lane / nbox;
+    const int b = lane - m * nbox;
+    fence_proxy_async_smem();
+    tma_load_3d(stg + (m * SROWS + st.slot + b * kSStep) * P, maps + m,
+                st.strip * kStrip - kLeft, st.h0() + b * kSStep, st.plane, bar);
+  }
+}
+
+// Horizontal pass of the streaming forward over staged rows [0, nh) of one slot, into moment
+// rows [0, nh) of `ring` (maps at column offsets 0: X, 64: X^2+Y^2, 128: Y, 192: XY). The
+// arithmetic is fwd_hpass's (merged second moment). L1: |x - y| of the centre pixels of
+// staged rows [l1_i0, l1_i1) in the strip's first l1_cols columns.
+template <int HALO, typename TIn>
+__device__ __forceinline__ void sfwd_hpass(const TIn* sx, const TIn* sy, float* ring, int nh,
+                                           const Taps2<HALO, HalfTaps<TIn>::value>& T, bool l1,
+                                           int l1_i0, int l1_i1, int l1_cols, float& l1_sum) {
+  constexpr int SP = StagePitch<TIn>::value;
+  constexpr int RP = RingPitch<4>::value;
+  constexpr int HA = (sizeof(TIn) == 2 || HALO > 4) ? 8 : 4;  // aligned left extent
+  constexpr int NV = 8 + 2 * HA;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int j = htask_chunk(warp, lane);
+#pragma unroll 1
+  for (int rg = 0; rg < nh; rg += kSStep) {
+    const int i = rg + htask_row(lane);
+    if (i < nh) {
+      {
+        float xv[NV], yv[NV];
+        load_vec(sx + i * SP + 8 * j + kLeft - HA, xv);
+        load_vec(sy + i * SP + 8 * j + kLeft - HA, yv);
+        PairRow<NV> X, Y, XX, S, XY;
+        X.build(xv);
+        Y.build(yv);
+#pragma unroll
+        for (int q = 0; q < NV / 2; ++q) {
+          XX.a[q] = mul2(X.a[q], X.a[q]);
+          XY.a[q] = mul2(X.a[q], Y.a[q]);
+          S.a[q] = fma2(Y.a[q], Y.a[q], XX.a[q]);
+        }
+        if (l1 && i >= l1_i0 && i < l1_i1) {
+          const int nc = l1_cols - 8 * j;  // centre columns of the task inside the image
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 dv = sub2(X.pr(HA + 2 * q), Y.pr(HA + 2 * q));
+            l1_sum += (2 * q < nc ? fabsf(dv.x) : 0.f) + (2 * q + 1 < nc ? fabsf(dv.y) : 0.f);
+          }
+        }
+        float* dst = ring + i * RP + 8 * j;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const int c = HA + 2 * p;  // first column of the output pair (even)
+          const float2 wc = T.w[HALO];
+          float2 sX = make_float2(0.f, 0.f), sY = sX, sXY = sX, sS = sX;
+#pragma unroll
+          for (int d = 1; d <= HALO; ++d) {
+            const float2 w = T.w[HALO - d];
+            sX = fma2(psum(X, c, d), w, sX);
+            sY = fma2(psum(Y, c, d), w, sY);
+            sXY = fma2(pfma(X, Y, XY, c, d), w, sXY);
+            sS = fma2(psum(S, c, d), w, sS);
+          }
+          *reinterpret_cast<float2*>(dst + 0 * kStrip + 2 * p) = fma2(X.pr(c), wc, sX);
+          *reinterpret_cast<float2*>(dst + 1 * kStrip + 2 * p) = fma2(S.pr(c), wc, sS);
+          *reinterpret_cast<float2*>(dst + 2 * kStrip + 2 * p) = fma2(Y.pr(c), wc, sY);
+          *reinterpret_cast<float2*>(dst + 3 * kStrip + 2 * p) = fma2(XY.pr(c), wc, sXY);
+        }
+      }
+    }
+  }
+}
+
+// Vertical 2*HALO+1 tap sum of output row k from window rows k..k+2*HALO (reference order:
+// pairs d = 1..HALO, centre last). `row(j)` returns window row j.
+template <int HALO, bool HW_, typename RowF>
+__device__ __forceinline__ float2 svsum(const Taps2<HALO, HW_>& T, int k, RowF row) {
+  float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int d = 1; d <= HALO; ++d) acc = fma2(add2(row(k + HALO - d), row(k + HALO + d)), T.w[HALO - d], acc);
+  return fma2(row(k + HALO), T.w[HALO], acc);
+}
+
+template <int HALO, bool HW_, typename RowF>
+__device__ __forceinline__ float svsum1(const Taps2<HALO, HW_>& T, int k, RowF row) {
+  float acc = 0.f;
+#pragma unroll
+  for (int d = 1; d <= HALO; ++d)
+    acc = __fmaf_rn(__fadd_rn(row(k + HALO - d), row(k + HALO + d)), T.w[HALO - d].x, acc);
+  return __fmaf_rn(row(k + HALO), T.w[HALO].x, acc);
+}
+
+struct PixelOut {
+  float v, pm, ps, pc;
+};
+
+// SSIM value and its three partials of two pixels from their four filtered moments (MERGED
+// form), each operand a pair of pixels (packed FP32, identical to the map kernels'
+// epilogue).
+struct PixelOut2 {
+  float2 v, pm, ps, pc;
+};
+template <bool TRAIN>
+__device__ __forceinline__ PixelOut2 ssim_pixel2(float2 mu1, float2 mu2, float2 S, float2 XY,
+                                                 float2 C1v, float2 C2v) {
+  const float2 neg1 = splat(-1.f), two = splat(2.f);
+  const float2 mu1_sq = mul2(mu1, mu1), mu2_sq = mul2(mu2, mu2);
+  const float2 msq = add2(mu1_sq, mu2_sq);
+  const float2 mu12 = mul2(mu1, mu2);
+  const float2 A = add2(msq, C1v);
+  const float2 B = add2(fma2(msq, neg1, S), C2v);
+  const float2 sigma12 = fma2(mu12, neg1, XY);
+  const float2 Cc = fma2(two, mu12, C1v);
+  const float2 D = fma2(two, sigma12, C2v);
+  const float2 rA = make_float2(rcp_approx(A.x), rcp_approx(A.y));
+  const float2 rB = make_float2(rcp_approx(B.x), rcp_approx(B.y));
+  const float2 rAB = mul2(rA, rB);
+  PixelOut2 o;
+  o.v = mul2(mul2(Cc, D), rAB);
+  if (TRAIN) {
+    o.pm = fma2(mul2(two, mu2), mul2(fma2(Cc, neg1, D), rAB),
+                mul2(mul2(two, mu1), mul2(o.v, fma2(rA, neg1, rB))));
+    o.ps = mul2(mul2(o.v, neg1), rB);
+    o.pc = mul2(mul2(two, Cc), rAB);
+  }
+  return o;
+}
+
+template <typename TP>
+__device__ __forceinline__ void store1(TP* p, float v) {
+  if constexpr (sizeof(TP) == 4) {
+    *p = v;
+  } else if constexpr (HalfTaps<TP>::value) {
+    *p = __float2half_rn(v);
+  } else {
+    *p = __float2bfloat16_rn(v);
+  }
+}
+
+// Last CTA of a reducing forward: turn the per-image fixed-point accumulators into the
+// outputs (NaN for every output of a call in which a CTA gave up), zero them again and, for
+// a sharded loss, publish the batch sum. Called by every thread of the CTA after its steps.
+template <int NT>
+__device__ __forceinline__ void finish_reduction(const FwdParams& a, bool failed, double* red,
+                                                 unsigned* s_last) {
+  const bool l1 = a.l1 != 0;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (failed) atomicOr(a.ticket + 1, 1u);  // the call's "failed" word
+    __threadfence();
+    const unsigned prev = atomicInc(a.ticket, gridDim.x - 1);
+    *s_last = (prev == gridDim.x - 1) ? 1u : 0u;
+  }
+  __syncthreads();
+  if (!*s_last) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) *s_last = atomicExch(a.ticket + 1, 0u) != 0u ? 2u : 1u;
+  __syncthreads();
+  const double poison = *s_last == 2u ? __longlong_as_double(0x7ff8000000000000ll) : 0.0;
+  double local = 0.0, local_l1 = 0.0;
+  for (int b = threadIdx.x; b < a.g.B; b += NT) {
+    const long long q = static_cast<long long>(atomicExch(a.acc + b, 0ull));
+    const double s = static_cast<double>(q) * (1.0 / kFixScale) + poison;
+    double s1 = 0.0;
+    if (l1) s1 = static_cast<double>(static_cast<long long>(atomicExch(a.acc_l1 + b, 0ull))) *
+                 (1.0 / kFixScaleL1);
+    if (a.image_sums) a.image_sums[b] = s;
+    if (a.reduce == 2)
+      a.out[b] = static_cast<float>(s * static_cast<double>(a.out_scale) +
+                                    s1 * static_cast<double>(a.l1_weight) +
+                                    static_cast<double>(a.out_offset));
+    local += s;
+    local_l1 += s1;
+  }
+  if (a.reduce == 1) {
+    const double total = block_sum_w<NT / 32>(local, red);
+    const double total_l1 = block_sum_w<NT / 32>(local_l1, red);
+    if (threadIdx.x == 0) {
+      a.out[0] = static_cast<float>(total * static_cast<double>(a.out_scale) +
+                                    total_l1 * static_cast<double>(a.l1_weight) +
+                                    static_cast<double>(a.out_offset));
+      if (a.dp.world > 0) dp_publish(a.dp, total);
+    }
+  }
+}
+
+template <int HALO, typename TIn, typename TP, bool TRAIN>
+struct SFwdConfig {
+  static constexpr bool kHalfW = HalfTaps<TIn>::value;
+  static constexpr int kSP = StagePitch<TIn>::value;
+  static constexpr int kRP = RingPitch<4>::value;
+  static constexpr int kRingRows = 2 * HALO > kSStep ? 2 * HALO : kSStep;
+  static_assert(2 * HALO <= 2 * kSStep, "a preload fits the two staging slots");
+  static constexpr size_t kStageBytes = 2ull * (2 * kSStep) * kSP * sizeof(TIn);  // 2 maps
+  static constexpr size_t kRingBytes = static_cast<size_t>(kRingRows) * kRP * sizeof(float);
+  static constexpr size_t kSmem = kStageBytes + kRingBytes + 128;
+  static constexpr int kFit = static_cast<int>((228 * 1024) / (kSmem + 1024));
+  static constexpr int kMinBlocks = kFit >= 8 ? 8 : kFit;
+};
+
+template <int HALO, typename TIn, typename TP, bool TRAIN>
+__global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::kMinBlocks))
+    loss_fwd_kernel(const __grid_constant__ FwdParams a) {
+  using Cfg = SFwdConfig<HALO, TIn, TP, TRAIN>;
+  constexpr int SP = Cfg::kSP;
+  constexpr int RP = Cfg::kRP;
+  constexpr int SROWS = 2 * kSStep;
+  constexpr bool HW_ = Cfg::kHalfW;
+  constexpr int W2 = 2 * HALO;  // window rows carried between steps
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
+  TIn* stg = reinterpret_cast<TIn*>(smem);
+  float* ring = reinterpret_cast<float*>(smem + Cfg::kStageBytes);
+  __shared__ double red[kSWarps];
+  __shared__ unsigned s_last;
+  __shared__ uint64_t bar;
+
+  const Geometry& g = a.g;
+  const int64_t beg = scta_range_start<HALO>(g, blockIdx.x, gridDim.x);
+  const int64_t end = scta_range_start<HALO>(g, blockIdx.x + 1, gridDim.x);
+  const TIn* const src[2] = {static_cast<const TIn*>(a.img1), static_cast<const TIn*>(a.img2)};
+  const int warp = threadIdx.x >> 5;
+  const int c = threadIdx.x;  // this thread's column in the strip
+  Taps2<HALO, HW_> T;
+  T.load();
+
+  const bool tma = a.use_tma != 0;
+  if (tma && threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  SStep<HALO> cur = sfirst_step<HALO>(beg, end, g);
+  if (tma && threadIdx.x < 2) prefetch_tensormap(a.tmap + threadIdx.x);
+  grid_dependency_wait();
+  grid_launch_dependents();
+  // staging of a step: TMA boxes issued by warp 0, or cp.async by the whole CTA
+  auto stage_step = [&](const SStep<HALO>& st) {
+    if (tma) {
+      if (warp == 0) sstage_tma<TIn, 2, HALO>(stg, a.tmap, st, &bar);
+    } else {
+      Step<HALO> s{};
+      s.plane = st.plane;
+      s.strip = st.strip;
+      s.first = false;
+      s.t = st.h0() - HALO;  // Step::h0() = t + HALO for a non-first step
+      s.n = st.nh();
+      stage<TIn, 2, SROWS, Step<HALO>, kSThreads>(stg + st.slot * SP, src, g, s, a.aligned16);
+    }
+  };
+  if (cur.live) stage_step(cur);
+  unsigned phase = 0;
+  double run_sum = 0.0, run_l1 = 0.0;
+  const bool l1 = a.l1 != 0;
+  bool failed = false;
+  float2 wP[W2], wQ[W2];  // the column's last 2*HALO moment rows: (X, Y), (X^2+Y^2, XY)
+#pragma unroll
+  for (int j = 0; j < W2; ++j) wP[j] = wQ[j] = make_float2(0.f, 0.f);
+  const int W = static_cast<int>(g.W);
+  const int H = static_cast<int>(g.H);
+  const float2 C1v = splat(a.C1), C2v = splat(a.C2);
+
+  while (cur.live) {
+    bool timed_out = false;
+    if (tma) {
+      timed_out = !mbar_wait_bounded(&bar, phase, a.wait_limit);
+      phase ^= 1u;
+    } else {
+      cp_async_wait_all();
+    }
+    if (__syncthreads_or(timed_out)) {
+      if (threadIdx.x == 0) atomicOr(&g_device_error, kErrStagingTimeout);
+      mbar_wait_bounded(&bar, phase ^ 1u, kWaitLimit);
+      failed = true;
+      break;
+    }
+    // The next regular step is staged into the other slot while this one is processed; a
+    // step next to a preload (which fills both slots) is staged after this horizontal pass.
+    const SStep<HALO> nxt = snext_step<HALO>(cur, g);
+    const bool early = nxt.live && !cur.pre && !nxt.pre;
+    if (early) stage_step(nxt);
+    float step_l1 = 0.f;
+    {
+      const int h0 = cur.h0();
+      const int l1_lo = cur.ps - h0;
+      const int l1_hi = cur.t_end - h0;
+      sfwd_hpass<HALO, TIn>(stg + cur.slot * SP, stg + (SROWS + cur.slot) * SP, ring, cur.nh(),
+                            T, l1, l1_lo > 0 ? l1_lo : 0, l1_hi, W - cur.strip * kStrip, step_l1);
+    }
+    run_l1 += static_cast<double>(step_l1);
+    __syncthreads();
+    if (nxt.live && !early) stage_step(nxt);
+
+    const float* col = ring + c;
+    if (cur.pre) {
+#pragma unroll
+      for (int j = 0; j < W2; ++j) {
+        wP[j] = make_float2(col[j * RP + 0 * kStrip], col[j * RP + 2 * kStrip]);
+        wQ[j] = make_float2(col[j * RP + 1 * kStrip], col[j * RP + 3 * kStrip]);
+      }
+    } else {
+      const int n = cur.n;
+      float2 nP[kSStep], nQ[kSStep];
+#pragma unroll
+      for (int r = 0; r < kSStep; ++r) {
+        if (r < n) {
+          nP[r] = make_float2(col[r * RP + 0 * kStrip], col[r * RP + 2 * kStrip]);
+          nQ[r] = make_float2(col[r * RP + 1 * kStrip], col[r * RP + 3 * kStrip]);
+        } else {
+          nP[r] = nQ[r] = make_float2(0.f, 0.f);
+        }
+      }
+      auto rowP = [&](int j) { return j < W2 ? wP[j] : nP[j - W2]; };
+      auto rowQ = [&](int j) { return j < W2 ? wQ[j] : nQ[j - W2]; };
+      const int gx = cur.strip * kStrip + c;
+      const bool in_x = gx < W;
+      const bool col_ok = in_x && (!a.valid || (gx >= HALO && gx < W - HALO));
+      const int64_t plane_off = static_cast<int64_t>(cur.plane) * g.HW;
+      const int off0 = cur.t * W + gx;  // 32-bit in-plane offset (planes < 2^31 elements)
+      float* mapp = a.map ? a.map + plane_off : nullptr;
+      TP* q0 = TRAIN ? static_cast<TP*>(a.p0) + plane_off : nullptr;
+      TP* q1 = TRAIN ? static_cast<TP*>(a.p1) + plane_off : nullptr;
+      TP* q2 = TRAIN ? static_cast<TP*>(a.p2) + plane_off : nullptr;
+      const int sx0 = cur.strip * kStrip;
+      const bool fast = n == kSStep && !a.clamp && sx0 + kStrip <= W &&
+                        (!a.valid || (cur.t >= HALO && cur.t + kSStep <= H - HALO &&
+                                      sx0 >= HALO && sx0 + kStrip <= W - HALO));
+      float step_sum = 0.f;
+      if (fast) {
+        // two output rows at a time: the epilogue runs on (row k, row k+1) pairs
+#pragma unroll
+        for (int k = 0; k < kSStep; k += 2) {
+          const float2 P0 = svsum<HALO, HW_>(T, k, rowP), P1 = svsum<HALO, HW_>(T, k + 1, rowP);
+          const float2 Q0 = svsum<HALO, HW_>(T, k, rowQ), Q1 = svsum<HALO, HW_>(T, k + 1, rowQ);
+          const PixelOut2 o = ssim_pixel2<TRAIN>(make_float2(P0.x, P1.x), make_float2(P0.y, P1.y),
+                                                 make_float2(Q0.x, Q1.x), make_float2(Q0.y, Q1.y),
+                                                 C1v, C2v);
+          if (a.reduce) step_sum += o.v.x + o.v.y;
+          const int off = off0 + k * W;
+          if (mapp) {
+            mapp[off] = o.v.x;
+            mapp[off + W] = o.v.y;
+          }
+          if (TRAIN) {
+            store1(q0 + off, o.pm.x);
+            store1(q0 + off + W, o.pm.y);
+            store1(q1 + off, o.ps.x);
+            store1(q1 + off + W, o.ps.y);
+            store1(q2 + off, o.pc.x);
+            store1(q2 + off + W, o.pc.y);
+          }
+        }
+      } else {
+        int rlo = 0, rhi = n;
+        if (a.valid) {
+          rlo = max(0, HALO - cur.t);
+          rhi = min(n, H - HALO - cur.t);
+        }
+#pragma unroll
+        for (int k = 0; k < kSStep; ++k) {
+          if (k < n) {
+            const float2 P = svsum<HALO, HW_>(T, k, rowP);
+            const float2 Q = svsum<HALO, HW_>(T, k, rowQ);
+            // the packed epilogue on the pixel twice (its first half is the result), the
+            // same instructions as the fast path's
+            const PixelOut2 o2 = ssim_pixel2<TRAIN>(splat(P.x), splat(P.y), splat(Q.x),
+                                                    splat(Q.y), C1v, C2v);
+            PixelOut o{o2.v.x, o2.pm.x, o2.ps.x, o2.pc.x};
+            const bool ok = col_ok && k >= rlo && k < rhi;
+            if (a.reduce) step_sum += (ok ? ((a.clamp && o.v < 0.f) ? 0.f : o.v) : 0.f);
+            if (in_x) {
+              const int off = off0 + k * W;
+              if (mapp) mapp[off] = o.v;
+              if (TRAIN) {
+                const bool live = !a.mask_partials || (ok && (!a.clamp || o.v >= 0.f));
+                if (!live) o.pm = o.ps = o.pc = 0.f;
+                store1(q0 + off, o.pm);
+                store1(q1 + off, o.ps);
+                store1(q2 + off, o.pc);
+              }
+            }
+          }
+        }
+      }
+      run_sum += static_cast<double>(step_sum);
+      // carry the window: the last 2*HALO of the window's and the step's rows (a partial
+      // step is the last of its part; the next step preloads a new window)
+      float2 cP[W2], cQ[W2];
+#pragma unroll
+      for (int j = 0; j < W2; ++j) {
+        cP[j] = rowP(j + kSStep);
+        cQ[j] = rowQ(j + kSStep);
+      }
+#pragma unroll
+      for (int j = 0; j < W2; ++j) {
+        wP[j] = cP[j];
+        wQ[j] = cQ[j];
+      }
+    }
+
+    if (a.reduce && cur.last()) {
+      // end of a column run part: fold its sums into the image's fixed-point accumulators
+      const double s = block_sum_w<kSWarps>(run_sum, red);
+      const double s1 = l1 ? block_sum_w<kSWarps>(run_l1, red) : 0.0;
+      run_sum = 0.0;
+      run_l1 = 0.0;
+      if (threadIdx.x == 0) {
+        atomicAdd(a.acc + cur.img, static_cast<unsigned long long>(__double2ll_rn(s * kFixScale)));
+        if (l1)
+          atomicAdd(a.acc_l1 + cur.img,
+                    static_cast<unsigned long long>(__double2ll_rn(s1 * kFixScaleL1)));
+      }
+    }
+    __syncthreads();  // the moment rows are consumed before the next step overwrites them
+    cur = nxt;
+  }
+
+  if (!a.reduce) return;
+  finish_reduction<kSThreads>(a, failed, red, &s_last);
+}
+
+// ---------------------------------------------------------------------------------------
+// Streaming backward: transposed Gaussian of the three partial maps, one column per thread
+// ---------------------------------------------------------------------------------------
+template <int HALO, typename TIn, typename TP>
+struct SBwdConfig {
+  static constexpr bool kHalfW = HalfTaps<TIn>::value;
+  static constexpr int kSP = StagePitch<TP>::value;
+  static constexpr int kRP = RingPitch<3>::value;
+  static constexpr int kRingRows = 2 * HALO > kSStep ? 2 * HALO : kSStep;
+  static constexpr size_t kStageBytes = 3ull * (2 * kSStep) * kSP * sizeof(TP);  // 3 maps
+  static constexpr size_t kRingBytes = static_cast<size_t>(kRingRows) * kRP * sizeof(float);
+  static constexpr size_t kSmem = kStageBytes + kRingBytes + 128;
+  static constexpr int kFit = static_cast<int>((228 * 1024) / (kSmem + 1024));
+  static constexpr int kMinBlocks = kFit >= 8 ? 8 : kFit;
+};
+
+// Horizontal pass of the streaming backward: the three staged partial maps, rows [0, nh).
+template <int HALO, typename TIn, typename TP>
+__device__ __forceinline__ void sbwd_hpass(const TP* sp, float* ring, int nh,
+                                           const Taps2<HALO, HalfTaps<TIn>::value>& T) {
+  constexpr int SP = StagePitch<TP>::value;
+  constexpr int RP = RingPitch<3>::value;
+  constexpr int SROWS = 2 * kSStep;
+  constexpr int HA = (sizeof(TP) == 2 || HALO > 4) ? 8 : 4;
+  constexpr int NV = 8 + 2 * HA;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int j = htask_chunk(warp, lane);
+#pragma unroll 1
+  for (int rg = 0; rg < nh; rg += kSStep) {
+    const int i = rg + htask_row(lane);
+    if (i < nh) {
+      {
+        float* dst = ring + i * RP + 8 * j;
+#pragma unroll
+        for (int m = 0; m < 3; ++m) {
+          float v[NV];
+          load_vec(sp + (m * SROWS + i) * SP + 8 * j + kLeft - HA, v);
+          PairRow<NV> V;
+          V.build(v);
+          float2 s4[4];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) s4[p] = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int d = 1; d <= HALO; ++d) {
+#pragma unroll
+            for (int p = 0; p < 4; ++p) s4[p] = fma2(psum(V, HA + 2 * p, d), T.w[HALO - d], s4[p]);
+          }
+#pragma unroll
+          for (int p = 0; p < 4; ++p)
+            *reinterpret_cast<float2*>(dst + m * kStrip + 2 * p) =
+                fma2(V.pr(HA + 2 * p), T.w[HALO], s4[p]);
+        }
+      }
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float ldg1(const T* p) {
+  if constexpr (sizeof(T) == 4) {
+    return __ldg(p);
+  } else {
+    return to_f(*p);
+  }
+}
+
+template <int HALO, typename TIn, typename TP>
+__global__ void __launch_bounds__(kSThreads, (SBwdConfig<HALO, TIn, TP>::kMinBlocks))
+    loss_bwd_kernel(const __grid_constant__ BwdParams a) {
+  using Cfg = SBwdConfig<HALO, TIn, TP>;
+  constexpr int SP = Cfg::kSP;
+  constexpr int RP = Cfg::kRP;
+  constexpr int SROWS = 2 * kSStep;
+  constexpr bool HW_ = Cfg::kHalfW;
+  constexpr int W2 = 2 * HALO;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
+  TP* stg = reinterpret_cast<TP*>(smem);
+  float* ring = reinterpret_cast<float*>(smem + Cfg::kStageBytes);
+  __shared__ uint64_t bar;
+
+  const Geometry& g = a.g;
+  const int64_t beg = scta_range_start<HALO>(g, blockIdx.x, gridDim.x);
+  const int64_t end = scta_range_start<HALO>(g, blockIdx.x + 1, gridDim.x);
+  const TP* const src[3] = {static_cast<const TP*>(a.p0), static_cast<const TP*>(a.p1),
+                            static_cast<const TP*>(a.p2)};
+  const TIn* img1 = static_cast<const TIn*>(a.img1);
+  const TIn* img2 = static_cast<const TIn*>(a.img2);
+  const int warp = threadIdx.x >> 5;
+  const int c = threadIdx.x;
+  Taps2<HALO, HW_> T;
+  T.load();
+
+  const bool tma = a.use_tma != 0;
+  if (tma && threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  SStep<HALO> cur = sfirst_step<HALO>(beg, end, g);
+  if (tma && threadIdx.x < 3) prefetch_tensormap(a.tmap + threadIdx.x);
+  grid_dependency_wait();
+  grid_launch_dependents();
+  auto stage_step = [&](const SStep<HALO>& st) {
+    if (tma) {
+      if (warp == 0) sstage_tma<TP, 3, HALO>(stg, a.tmap, st, &bar);
+    } else {
+      Step<HALO> s{};
+      s.plane = st.plane;
+      s.strip = st.strip;
+      s.first = false;
+      s.t = st.h0() - HALO;
+      s.n = st.nh();
+      stage<TP, 3, SROWS, Step<HALO>, kSThreads>(stg + st.slot * SP, src, g, s, a.aligned16);
+    }
+  };
+  if (cur.live) stage_step(cur);
+  unsigned phase = 0;
+  float2 wA[W2];  // the column's last 2*HALO rows of filtered (dm_dmu1, dm_dsigma1_sq)
+  float wB[W2];   // ... and of filtered dm_dsigma12
+#pragma unroll
+  for (int j = 0; j < W2; ++j) {
+    wA[j] = make_float2(0.f, 0.f);
+    wB[j] = 0.f;
+  }
+  const int W = static_cast<int>(g.W);
+
+  while (cur.live) {
+    bool timed_out = false;
+    if (tma) {
+      timed_out = !mbar_wait_bounded(&bar, phase, a.wait_limit);
+      phase ^= 1u;
+    } else {
+      cp_async_wait_all();
+    }
+    if (__syncthreads_or(timed_out)) {
+      if (threadIdx.x == 0) atomicOr(&g_device_error, kErrStagingTimeout);
+      mbar_wait_bounded(&bar, phase ^ 1u, kWaitLimit);
+      return;
+    }
+    const SStep<HALO> nxt = snext_step<HALO>(cur, g);
+    const bool early = nxt.live && !cur.pre && !nxt.pre;
+    if (early) stage_step(nxt);
+    // the epilogue's image values, loaded before the horizontal pass so they are in flight
+    const int gx = cur.strip * kStrip + c;
+    const bool in_x = gx < W;
+    const int64_t plane_off = static_cast<int64_t>(cur.plane) * g.HW;
+    const int off0 = cur.t * W + gx;
+    float xin[kSStep], yin[kSStep];
+    if (!cur.pre) {
+      const TIn* x_pl = img1 + plane_off;
+      const TIn* y_pl = img2 + plane_off;
+#pragma unroll
+      for (int k = 0; k < kSStep; ++k) {
+        const bool ld = in_x && k < cur.n;
+        xin[k] = ld ? ldg1(x_pl + off0 + k * W) : 0.f;
+        yin[k] = ld ? ldg1(y_pl + off0 + k * W) : 0.f;
+      }
+    }
+    sbwd_hpass<HALO, TIn, TP>(stg + cur.slot * SP, ring, cur.nh(), T);
+    __syncthreads();
+    if (nxt.live && !early) stage_step(nxt);
+
+    const float* col = ring + c;
+    if (cur.pre) {
+#pragma unroll
+      for (int j = 0; j < W2; ++j) {
+        wA[j] = make_float2(col[j * RP + 0 * kStrip], col[j * RP + 1 * kStrip]);
+        wB[j] = col[j * RP + 2 * kStrip];
+      }
+    } else {
+      const int n = cur.n;
+      float2 nA[kSStep];
+      float nB[kSStep];
+#pragma unroll
+      for (int r = 0; r < kSStep; ++r) {
+        if (r < n) {
+          nA[r] = make_float2(col[r * RP + 0 * kStrip], col[r * RP + 1 * kStrip]);
+          nB[r] = col[r * RP + 2 * kStrip];
+        } else {
+          nA[r] = make_float2(0.f, 0.f);
+          nB[r] = 0.f;
+        }
+      }
+      auto rowA = [&](int j) { return j < W2 ? wA[j] : nA[j - W2]; };
+      auto rowB = [&](int j) { return j < W2 ? wB[j] : nB[j - W2]; };
+      float chain = a.chain_scale;
+      float l1c = a.l1_scale;
+      if (a.grad_out) {
+        const float up = a.grad_out[a.grad_per_image ? cur.img : 0];
+        chain = __fmul_rn(chain, up);
+        l1c = __fmul_rn(l1c, up);
+      }
+      float gv[kSStep];
+#pragma unroll
+      for (int k = 0; k < kSStep; ++k) {
+        const float2 r01 = svsum<HALO, HW_>(T, k, rowA);
+        const float r2 = svsum1<HALO, HW_>(T, k, rowB);
+        // g = s0 + 2 x s1 + y s2 (csrc/ssim.cu:504), then the chain factor
+        gv[k] = __fmul_rn(__fmaf_rn(yin[k], r2, __fmaf_rn(__fmul_rn(2.f, xin[k]), r01.y, r01.x)),
+                          chain);
+      }
+      if (a.l1_scale != 0.f) {
+        // d|x - y|/dx = sign(x - y), 0 where x == y (torch's abs backward)
+#pragma unroll
+        for (int k = 0; k < kSStep; ++k) {
+          const float dv = __fsub_rn(xin[k], yin[k]);
+          gv[k] = __fmaf_rn(dv > 0.f ? 1.f : (dv < 0.f ? -1.f : 0.f), l1c, gv[k]);
+        }
+      }
+      auto store_grad = [&](auto* base) {
+        auto* gp = base + plane_off;
+        if (n == kSStep && in_x) {
+#pragma unroll
+          for (int k = 0; k < kSStep; ++k) store1(gp + off0 + k * W, gv[k]);
+        } else if (in_x) {
+#pragma unroll
+          for (int k = 0; k < kSStep; ++k)
+            if (k < n) store1(gp + off0 + k * W, gv[k]);
+        }
+      };
+      if (a.grad_dtype == 0)
+        store_grad(static_cast<float*>(a.grad));
+      else if (a.grad_dtype == 1)
+        store_grad(static_cast<__half*>(a.grad));
+      else
+        store_grad(static_cast<__nv_bfloat16*>(a.grad));
+      float2 cA[W2];
+      float cB[W2];
+#pragma unroll
+      for (int j = 0; j < W2; ++j) {
+        cA[j] = rowA(j + kSStep);
+        cB[j] = rowB(j + kSStep);
+      }
+#pragma unroll
+      for (int j = 0; j < W2; ++j) {
+        wA[j] = cA[j];
+        wB[j] = cB[j];
+      }
+    }
+    __syncthreads();
+    cur = nxt;
+  }
+}
+
+}  // namespace fssim

@@ -483,6 +483,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     check_status(fssim_poll_device_error(&code, clear ? 1 : 0));
     return static_cast<int64_t>(code);
   });
+  m.def("set_loss_kernels", [](int family) { check_status(fssim_set_loss_kernels(family)); });
   m.def("set_staging_wait_limit", [](int64_t polls) {
     check_status(fssim_set_staging_wait_limit(static_cast<long long>(polls)));
   });

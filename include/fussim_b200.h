@@ -82,6 +82,17 @@ int fssim_set_staging_wait_limit(long long polls);
  * Applies to launches made after the call; process-wide. */
 int fssim_set_gather_timeout_us(long long us);
 
+/* Kernels of the fused loss path (fssim_forward, fssim_backward and the sharded forward).
+ * Both families compute bitwise-identical per-pixel results (partials, gradients, maps):
+ *  FSSIM_KERNELS_STREAM (default): 64-thread CTAs, one output column per thread, the
+ *      vertical filter window carried in registers from step to step;
+ *  FSSIM_KERNELS_TILE: 128-thread CTAs computing 2-column x 4-row tiles, the vertical halo
+ *      kept in shared memory (the kernels of the map entry points in section 1).
+ * Process-wide; applies to launches made after the call (FSSIM_ERR_ARGUMENT otherwise). */
+#define FSSIM_KERNELS_STREAM 0
+#define FSSIM_KERNELS_TILE 1
+int fssim_set_loss_kernels(int family);
+
 /* Number of SMs the kernels' persistent grids leave unused (default 0), for callers that
  * run another kernel concurrently, e.g. a collective overlapping the backward: a grid that
  * fills every SM would otherwise wait for that kernel's blocks to leave before its last
