@@ -348,10 +348,20 @@ int launch_sbwd(const fssim::BwdParams& p, cudaStream_t stream) {
 }
 
 // Kernel family of the fused loss path (fssim_set_loss_kernels): the column-streaming
-// kernels (FSSIM_KERNELS_STREAM, default) or the 4-row tile kernels that the map entry
-// points use (FSSIM_KERNELS_TILE).
-std::atomic<int> g_loss_kernels{FSSIM_KERNELS_STREAM};
-bool loss_streaming() { return g_loss_kernels.load(std::memory_order_relaxed) == FSSIM_KERNELS_STREAM; }
+// kernels, the 4-row tile kernels that the map entry points use, or (default) per launch
+// the family that measured faster on a B200 for its size (CUDA events, FP32 and FP16,
+// windows 7 and 11): the streaming kernels, except the tile kernels below 2^21
+// channel-pixels (1x3x256^2: 8.4 + 5.1 us against 13.0 + 8.6 us; the streaming kernels'
+// 8-row steps leave a short grid more latency-bound) and the tile backward from 2^27
+// channel-pixels (16x3x2048^2: 1084 us against 1157 us).
+std::atomic<int> g_loss_kernels{FSSIM_KERNELS_AUTO};
+constexpr int64_t kStreamMinCpx = int64_t{1} << 21;
+constexpr int64_t kStreamBwdMaxCpx = int64_t{1} << 27;
+bool loss_streaming(bool forward, int64_t cpx) {
+  const int f = g_loss_kernels.load(std::memory_order_relaxed);
+  if (f == FSSIM_KERNELS_AUTO) return cpx >= kStreamMinCpx && (forward || cpx < kStreamBwdMaxCpx);
+  return f == FSSIM_KERNELS_STREAM;
+}
 
 template <typename TIn, typename TP, bool TRAIN>
 int dispatch_loss_fwd(int ws, const fssim::FwdParams& p, cudaStream_t s, bool streaming) {
@@ -519,8 +529,10 @@ int fssim_set_reserved_sms(int n) {
 
 int fssim_set_loss_kernels(int family) {
   g_last_error.clear();
-  if (family != FSSIM_KERNELS_STREAM && family != FSSIM_KERNELS_TILE)
-    return fail(FSSIM_ERR_ARGUMENT, "family must be FSSIM_KERNELS_STREAM or FSSIM_KERNELS_TILE");
+  if (family != FSSIM_KERNELS_STREAM && family != FSSIM_KERNELS_TILE &&
+      family != FSSIM_KERNELS_AUTO)
+    return fail(FSSIM_ERR_ARGUMENT,
+                "family must be FSSIM_KERNELS_STREAM, FSSIM_KERNELS_TILE or FSSIM_KERNELS_AUTO");
   g_loss_kernels.store(family, std::memory_order_relaxed);
   return FSSIM_OK;
 }
@@ -698,7 +710,7 @@ int forward_impl(const fssim_forward_args* a, const fssim::DpParams* dp, cudaStr
   if (a->train) pair = pair && aligned(p.p0, 2 * PE) && aligned(p.p1, 2 * PE) && aligned(p.p2, 2 * PE);
   p.pair_ok = pair;
   // the family is read once: its tensor maps' box height must match the kernels launched
-  const bool streaming = loss_streaming();
+  const bool streaming = loss_streaming(true, N);
   set_fwd_tma(p, E, streaming ? fssim::kSStep : fssim::kBoxRows);
   if (dp) p.dp = *dp;
 
@@ -874,7 +886,7 @@ int fssim_backward(const fssim_backward_args* a, fssim_stream_t stream) {
                 aligned(p.p1, 16) && aligned(p.p2, 16);
   p.pair_ok = (a->W % 2 == 0) && aligned(a->img1, 2 * E) && aligned(a->img2, 2 * E) &&
               aligned(a->grad, 2 * GE);
-  const bool streaming = loss_streaming();
+  const bool streaming = loss_streaming(false, N);
   set_bwd_tma(p, PE, streaming ? fssim::kSStep : fssim::kBoxRows);
   const int ws = a->window_size;
   cudaStream_t s = stream;

@@ -57,88 +57,6 @@ __device__ __forceinline__ double block_sum_w(double v, double* red) {
   return s;
 }
 
-// One step of a streaming kernel: the first step of a run part preloads the window (moment
-// rows [t - HALO, t + HALO), no outputs); a regular step produces output rows [t, t + n)
-// from the new moment rows [t + HALO, t + HALO + n). Staging: a regular step's rows fill one
-// of two slots of kSStep rows, a preload's 2*HALO rows both slots.
-template <int HALO>
-struct SStep {
-  int plane, img, chan, strip;
-  int t;      // first output row of the step (of the part, for a preload)
-  int n;      // output rows of the regular step (1..kSStep)
-  int ps;     // first output row of the part
-  int t_end;  // end row of the CTA's part of this column run
-  int rest;   // strip-rows of the CTA's range after that part
-  int slot;   // first staging row (0 or kSStep)
-  bool pre;   // preload step
-  bool live;  // false: no step
-  __device__ __forceinline__ int h0() const { return pre ? t - HALO : t + HALO; }
-  __device__ __forceinline__ int nh() const { return pre ? 2 * HALO : n; }
-  __device__ __forceinline__ bool last() const { return !pre && t + n == t_end; }
-};
-
-template <int HALO>
-__device__ __forceinline__ SStep<HALO> sfirst_step(int64_t beg, int64_t end, const Geometry& g) {
-  SStep<HALO> s;
-  const int64_t len = end - beg;
-  s.live = len > 0;
-  if (!s.live) return s;
-  const int64_t col = beg / g.H;
-  s.t = static_cast<int>(beg - col * g.H);
-  const int64_t plane = col / g.S;
-  s.plane = static_cast<int>(plane);
-  s.strip = static_cast<int>(col - plane * g.S);
-  s.img = s.plane / g.C;
-  s.chan = s.plane - s.img * g.C;
-  const int64_t seg = (g.H - s.t) < len ? (g.H - s.t) : len;
-  s.ps = s.t;
-  s.t_end = s.t + static_cast<int>(seg);
-  s.rest = static_cast<int>(len - seg);
-  s.slot = 0;
-  s.pre = true;
-  s.n = static_cast<int>(seg) < kSStep ? static_cast<int>(seg) : kSStep;
-  return s;
-}
-
-// The step after c. Its staging slot: 0 after a preload and for a preload (which are staged
-// once the previous step's horizontal pass is done), else the slot c does not use.
-template <int HALO>
-__device__ __forceinline__ SStep<HALO> snext_step(const SStep<HALO>& c, const Geometry& g) {
-  SStep<HALO> s = c;
-  if (c.pre) {  // the part's first regular step, at the same rows
-    s.pre = false;
-    s.slot = 0;
-    return s;
-  }
-  s.slot = c.slot ^ kSStep;
-  s.t = c.t + c.n;
-  if (s.t == c.t_end) {  // the CTA's part of this column run is done
-    if (c.rest == 0) {
-      s.live = false;
-      return s;
-    }
-    s.t = 0;
-    s.ps = 0;
-    s.pre = true;
-    s.slot = 0;
-    if (++s.strip == g.S) {
-      s.strip = 0;
-      ++s.plane;
-      if (++s.chan == g.C) {
-        s.chan = 0;
-        ++s.img;
-      }
-    }
-    const int H = static_cast<int>(g.H);
-    const int seg = c.rest < H ? c.rest : H;
-    s.t_end = seg;
-    s.rest = c.rest - seg;
-  }
-  const int r = s.t_end - s.t;
-  s.n = r < kSStep ? r : kSStep;
-  return s;
-}
-
 // Start of CTA b's range of strip-rows for the streaming kernels: as cta_range_start, with a
 // run part costing its rows plus the 2*HALO rows of its preload.
 template <int HALO>
@@ -152,6 +70,57 @@ __device__ __forceinline__ int64_t scta_range_start(const Geometry& g, int64_t b
   return r * g.H + (o / kSStep) * kSStep;
 }
 
+// A CTA's part of one column run: plane (image img, channel chan), strip, output rows
+// [t0, t1); rest = strip-rows of the CTA's range after this part.
+struct SPart {
+  int plane, img, chan, strip, t0, t1, rest;
+  bool live;
+};
+
+__device__ __forceinline__ SPart sfirst_part(int64_t beg, int64_t end, const Geometry& g) {
+  SPart p;
+  const int64_t len = end - beg;
+  p.live = len > 0;
+  if (!p.live) return p;
+  const int64_t col = beg / g.H;
+  p.t0 = static_cast<int>(beg - col * g.H);
+  const int64_t plane = col / g.S;
+  p.plane = static_cast<int>(plane);
+  p.strip = static_cast<int>(col - plane * g.S);
+  p.img = p.plane / g.C;
+  p.chan = p.plane - p.img * g.C;
+  const int64_t seg = (g.H - p.t0) < len ? (g.H - p.t0) : len;
+  p.t1 = p.t0 + static_cast<int>(seg);
+  p.rest = static_cast<int>(len - seg);
+  return p;
+}
+
+__device__ __forceinline__ SPart snext_part(const SPart& c, const Geometry& g) {
+  SPart p = c;
+  if (!c.live || c.rest == 0) {
+    p.live = false;
+    return p;
+  }
+  if (++p.strip == g.S) {
+    p.strip = 0;
+    ++p.plane;
+    if (++p.chan == g.C) {
+      p.chan = 0;
+      ++p.img;
+    }
+  }
+  const int H = static_cast<int>(g.H);
+  p.t0 = 0;
+  p.t1 = c.rest < H ? c.rest : H;
+  p.rest = c.rest - p.t1;
+  return p;
+}
+
+// Rows [h0, h0 + nh) (nh <= 2 * kSStep) of one strip of one plane, into staging slot `slot`.
+struct SStage {
+  int plane, strip, h0, nh, slot;
+};
+
 // Bytes the TMA staging of nh rows delivers for NMAP maps of element type T (boxes of
 // kSStep rows).
 template <typename T, int NMAP>
@@ -162,20 +131,20 @@ __device__ __forceinline__ unsigned sstep_bytes(int nh) {
 
 // TMA staging of step st by the lanes of warp 0: lane m * nbox + b copies box b (kSStep rows)
 // of map m into rows [slot + b * kSStep, ...) of the layout [NMAP][2 * kSStep][pitch].
-template <typename T, int NMAP, int HALO>
-__device__ __forceinline__ void sstage_tma(T* stg, const CUtensorMap* maps, const SStep<HALO>& st,
+template <typename T, int NMAP>
+__device__ __forceinline__ void sstage_tma(T* stg, const CUtensorMap* maps, const SStage& st,
                                            uint64_t* bar) {
   constexpr int P = StagePitch<T>::value;
   constexpr int SROWS = 2 * kSStep;
   const int lane = threadIdx.x & 31;
-  const int nbox = (st.nh() + kSStep - 1) / kSStep;
-  if (lane == 0) mbar_arrive_expect_tx(bar, sstep_bytes<T, NMAP>(st.nh()));
+  const int nbox = (st.nh + kSStep - 1) / kSStep;
+  if (lane == 0) mbar_arrive_expect_tx(bar, sstep_bytes<T, NMAP>(st.nh));
   if (lane < NMAP * nbox) {
     const int m = lane / nbox;
     const int b = lane - m * nbox;
     fence_proxy_async_smem();
     tma_load_3d(stg + (m * SROWS + st.slot + b * kSStep) * P, maps + m,
-                st.strip * kStrip - kLeft, st.h0() + b * kSStep, st.plane, bar);
+                st.strip * kStrip - kLeft, st.h0 + b * kSStep, st.plane, bar);
   }
 }
 
@@ -367,7 +336,8 @@ struct SFwdConfig {
   static constexpr size_t kRingBytes = static_cast<size_t>(kRingRows) * kRP * sizeof(float);
   static constexpr size_t kSmem = kStageBytes + kRingBytes + 128;
   static constexpr int kFit = static_cast<int>((228 * 1024) / (kSmem + 1024));
-  static constexpr int kMinBlocks = kFit >= 8 ? 8 : kFit;
+  // 7 CTAs/SM: a register budget of 146 holds the window and the part's pointers unspilled
+  static constexpr int kMinBlocks = kFit >= 6 ? 6 : kFit;
 };
 
 template <int HALO, typename TIn, typename TP, bool TRAIN>
@@ -402,37 +372,27 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
     fence_mbar_init();
   }
   __syncthreads();
-  SStep<HALO> cur = sfirst_step<HALO>(beg, end, g);
+  SPart part = sfirst_part(beg, end, g);
   if (tma && threadIdx.x < 2) prefetch_tensormap(a.tmap + threadIdx.x);
   grid_dependency_wait();
   grid_launch_dependents();
-  // staging of a step: TMA boxes issued by warp 0, or cp.async by the whole CTA
-  auto stage_step = [&](const SStep<HALO>& st) {
+  // staging of rows: TMA boxes issued by warp 0, or cp.async by the whole CTA
+  auto stage_rows = [&](const SStage& st) {
     if (tma) {
-      if (warp == 0) sstage_tma<TIn, 2, HALO>(stg, a.tmap, st, &bar);
+      if (warp == 0) sstage_tma<TIn, 2>(stg, a.tmap, st, &bar);
     } else {
       Step<HALO> s{};
       s.plane = st.plane;
       s.strip = st.strip;
       s.first = false;
-      s.t = st.h0() - HALO;  // Step::h0() = t + HALO for a non-first step
-      s.n = st.nh();
+      s.t = st.h0 - HALO;  // Step::h0() = t + HALO for a non-first step
+      s.n = st.nh;
       stage<TIn, 2, SROWS, Step<HALO>, kSThreads>(stg + st.slot * SP, src, g, s, a.aligned16);
     }
   };
-  if (cur.live) stage_step(cur);
   unsigned phase = 0;
-  double run_sum = 0.0, run_l1 = 0.0;
-  const bool l1 = a.l1 != 0;
-  bool failed = false;
-  float2 wP[W2], wQ[W2];  // the column's last 2*HALO moment rows: (X, Y), (X^2+Y^2, XY)
-#pragma unroll
-  for (int j = 0; j < W2; ++j) wP[j] = wQ[j] = make_float2(0.f, 0.f);
-  const int W = static_cast<int>(g.W);
-  const int H = static_cast<int>(g.H);
-  const float2 C1v = splat(a.C1), C2v = splat(a.C2);
-
-  while (cur.live) {
+  // wait for the staging in flight; false (the CTA stops) if the copy did not arrive
+  auto wait_staged = [&]() -> bool {
     bool timed_out = false;
     if (tma) {
       timed_out = !mbar_wait_bounded(&bar, phase, a.wait_limit);
@@ -443,62 +403,89 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
     if (__syncthreads_or(timed_out)) {
       if (threadIdx.x == 0) atomicOr(&g_device_error, kErrStagingTimeout);
       mbar_wait_bounded(&bar, phase ^ 1u, kWaitLimit);
+      return false;
+    }
+    return true;
+  };
+  if (part.live) stage_rows({part.plane, part.strip, part.t0 - HALO, W2, 0});
+  const bool l1 = a.l1 != 0;
+  bool failed = false;
+  const int W = static_cast<int>(g.W);
+  const int H = static_cast<int>(g.H);
+  const float2 C1v = splat(a.C1), C2v = splat(a.C2);
+  const float* col = ring + c;
+
+  while (part.live) {
+    const SPart nextp = snext_part(part, g);
+    // ---- constants of the part ----
+    const int sx0 = part.strip * kStrip;
+    const int gx = sx0 + c;
+    const bool in_x = gx < W;
+    const bool col_ok = in_x && (!a.valid || (gx >= HALO && gx < W - HALO));
+    const bool strip_fast = !a.clamp && sx0 + kStrip <= W &&
+                            (!a.valid || (sx0 >= HALO && sx0 + kStrip <= W - HALO));
+    const int64_t plane_off = static_cast<int64_t>(part.plane) * g.HW;
+    float* mapp = a.map ? a.map + plane_off + gx : nullptr;
+    TP* q0 = TRAIN ? static_cast<TP*>(a.p0) + plane_off + gx : nullptr;
+    TP* q1 = TRAIN ? static_cast<TP*>(a.p1) + plane_off + gx : nullptr;
+    TP* q2 = TRAIN ? static_cast<TP*>(a.p2) + plane_off + gx : nullptr;
+    const int l1_cols = W - sx0;
+    double run_sum = 0.0, run_l1 = 0.0;
+
+    // ---- preload: moment rows [t0 - HALO, t0 + HALO) fill the window ----
+    if (!wait_staged()) {
       failed = true;
       break;
     }
-    // The next regular step is staged into the other slot while this one is processed; a
-    // step next to a preload (which fills both slots) is staged after this horizontal pass.
-    const SStep<HALO> nxt = snext_step<HALO>(cur, g);
-    const bool early = nxt.live && !cur.pre && !nxt.pre;
-    if (early) stage_step(nxt);
-    float step_l1 = 0.f;
     {
-      const int h0 = cur.h0();
-      const int l1_lo = cur.ps - h0;
-      const int l1_hi = cur.t_end - h0;
-      sfwd_hpass<HALO, TIn>(stg + cur.slot * SP, stg + (SROWS + cur.slot) * SP, ring, cur.nh(),
-                            T, l1, l1_lo > 0 ? l1_lo : 0, l1_hi, W - cur.strip * kStrip, step_l1);
+      float l1s = 0.f;
+      sfwd_hpass<HALO, TIn>(stg, stg + SROWS * SP, ring, W2, T, l1, HALO,
+                            part.t1 - part.t0 + HALO, l1_cols, l1s);
+      run_l1 += static_cast<double>(l1s);
     }
-    run_l1 += static_cast<double>(step_l1);
     __syncthreads();
-    if (nxt.live && !early) stage_step(nxt);
+    // the first regular step's rows fill slot 0 (the preload used both slots)
+    stage_rows({part.plane, part.strip, part.t0 + HALO, min(kSStep, part.t1 - part.t0), 0});
+    float2 wP[W2], wQ[W2];  // the column's last 2*HALO moment rows: (X, Y), (X^2+Y^2, XY)
+#pragma unroll
+    for (int j = 0; j < W2; ++j) {
+      wP[j] = make_float2(col[j * RP + 0 * kStrip], col[j * RP + 2 * kStrip]);
+      wQ[j] = make_float2(col[j * RP + 1 * kStrip], col[j * RP + 3 * kStrip]);
+    }
+    __syncthreads();
 
-    const float* col = ring + c;
-    if (cur.pre) {
-#pragma unroll
-      for (int j = 0; j < W2; ++j) {
-        wP[j] = make_float2(col[j * RP + 0 * kStrip], col[j * RP + 2 * kStrip]);
-        wQ[j] = make_float2(col[j * RP + 1 * kStrip], col[j * RP + 3 * kStrip]);
+    // ---- regular steps: output rows [t, t + n) ----
+    int slot = 0;
+    for (int t = part.t0; t < part.t1; t += kSStep) {
+      const int n = min(kSStep, part.t1 - t);
+      const bool last = t + kSStep >= part.t1;
+      if (!wait_staged()) {
+        failed = true;
+        break;
       }
-    } else {
-      const int n = cur.n;
+      if (!last) stage_rows({part.plane, part.strip, t + kSStep + HALO,
+                             min(kSStep, part.t1 - t - kSStep), slot ^ kSStep});
+      {
+        float l1s = 0.f;
+        sfwd_hpass<HALO, TIn>(stg + slot * SP, stg + (SROWS + slot) * SP, ring, n, T, l1, 0,
+                              part.t1 - t - HALO, l1_cols, l1s);
+        run_l1 += static_cast<double>(l1s);
+      }
+      __syncthreads();
+      // the next part's preload fills both slots once this step's rows are consumed
+      if (last && nextp.live) stage_rows({nextp.plane, nextp.strip, nextp.t0 - HALO, W2, 0});
+
       float2 nP[kSStep], nQ[kSStep];
+      const int off0 = t * W;  // 32-bit in-plane row offset (planes < 2^31 elements)
+      float step_sum = 0.f;
+      if (n == kSStep && strip_fast && (!a.valid || (t >= HALO && t + kSStep <= H - HALO))) {
 #pragma unroll
-      for (int r = 0; r < kSStep; ++r) {
-        if (r < n) {
+        for (int r = 0; r < kSStep; ++r) {
           nP[r] = make_float2(col[r * RP + 0 * kStrip], col[r * RP + 2 * kStrip]);
           nQ[r] = make_float2(col[r * RP + 1 * kStrip], col[r * RP + 3 * kStrip]);
-        } else {
-          nP[r] = nQ[r] = make_float2(0.f, 0.f);
         }
-      }
-      auto rowP = [&](int j) { return j < W2 ? wP[j] : nP[j - W2]; };
-      auto rowQ = [&](int j) { return j < W2 ? wQ[j] : nQ[j - W2]; };
-      const int gx = cur.strip * kStrip + c;
-      const bool in_x = gx < W;
-      const bool col_ok = in_x && (!a.valid || (gx >= HALO && gx < W - HALO));
-      const int64_t plane_off = static_cast<int64_t>(cur.plane) * g.HW;
-      const int off0 = cur.t * W + gx;  // 32-bit in-plane offset (planes < 2^31 elements)
-      float* mapp = a.map ? a.map + plane_off : nullptr;
-      TP* q0 = TRAIN ? static_cast<TP*>(a.p0) + plane_off : nullptr;
-      TP* q1 = TRAIN ? static_cast<TP*>(a.p1) + plane_off : nullptr;
-      TP* q2 = TRAIN ? static_cast<TP*>(a.p2) + plane_off : nullptr;
-      const int sx0 = cur.strip * kStrip;
-      const bool fast = n == kSStep && !a.clamp && sx0 + kStrip <= W &&
-                        (!a.valid || (cur.t >= HALO && cur.t + kSStep <= H - HALO &&
-                                      sx0 >= HALO && sx0 + kStrip <= W - HALO));
-      float step_sum = 0.f;
-      if (fast) {
+        auto rowP = [&](int j) { return j < W2 ? wP[j] : nP[j - W2]; };
+        auto rowQ = [&](int j) { return j < W2 ? wQ[j] : nQ[j - W2]; };
         // two output rows at a time: the epilogue runs on (row k, row k+1) pairs
 #pragma unroll
         for (int k = 0; k < kSStep; k += 2) {
@@ -523,10 +510,21 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
           }
         }
       } else {
+#pragma unroll
+        for (int r = 0; r < kSStep; ++r) {
+          if (r < n) {
+            nP[r] = make_float2(col[r * RP + 0 * kStrip], col[r * RP + 2 * kStrip]);
+            nQ[r] = make_float2(col[r * RP + 1 * kStrip], col[r * RP + 3 * kStrip]);
+          } else {
+            nP[r] = nQ[r] = make_float2(0.f, 0.f);
+          }
+        }
+        auto rowP = [&](int j) { return j < W2 ? wP[j] : nP[j - W2]; };
+        auto rowQ = [&](int j) { return j < W2 ? wQ[j] : nQ[j - W2]; };
         int rlo = 0, rhi = n;
         if (a.valid) {
-          rlo = max(0, HALO - cur.t);
-          rhi = min(n, H - HALO - cur.t);
+          rlo = max(0, HALO - t);
+          rhi = min(n, H - HALO - t);
         }
 #pragma unroll
         for (int k = 0; k < kSStep; ++k) {
@@ -555,36 +553,38 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
         }
       }
       run_sum += static_cast<double>(step_sum);
-      // carry the window: the last 2*HALO of the window's and the step's rows (a partial
-      // step is the last of its part; the next step preloads a new window)
-      float2 cP[W2], cQ[W2];
+      // carry the window: the last 2*HALO rows of window and step (after a partial step,
+      // the last of its part, the next part preloads a new window)
+      {
+        float2 cP[W2], cQ[W2];
 #pragma unroll
-      for (int j = 0; j < W2; ++j) {
-        cP[j] = rowP(j + kSStep);
-        cQ[j] = rowQ(j + kSStep);
-      }
+        for (int j = 0; j < W2; ++j) {
+          cP[j] = j + kSStep < W2 ? wP[j + kSStep] : nP[j + kSStep - W2];
+          cQ[j] = j + kSStep < W2 ? wQ[j + kSStep] : nQ[j + kSStep - W2];
+        }
 #pragma unroll
-      for (int j = 0; j < W2; ++j) {
-        wP[j] = cP[j];
-        wQ[j] = cQ[j];
+        for (int j = 0; j < W2; ++j) {
+          wP[j] = cP[j];
+          wQ[j] = cQ[j];
+        }
       }
-    }
-
-    if (a.reduce && cur.last()) {
-      // end of a column run part: fold its sums into the image's fixed-point accumulators
-      const double s = block_sum_w<kSWarps>(run_sum, red);
-      const double s1 = l1 ? block_sum_w<kSWarps>(run_l1, red) : 0.0;
-      run_sum = 0.0;
-      run_l1 = 0.0;
-      if (threadIdx.x == 0) {
-        atomicAdd(a.acc + cur.img, static_cast<unsigned long long>(__double2ll_rn(s * kFixScale)));
-        if (l1)
-          atomicAdd(a.acc_l1 + cur.img,
-                    static_cast<unsigned long long>(__double2ll_rn(s1 * kFixScaleL1)));
+      if (a.reduce && last) {
+        // end of the part: fold its sums into the image's fixed-point accumulators
+        const double s_ = block_sum_w<kSWarps>(run_sum, red);
+        const double s1 = l1 ? block_sum_w<kSWarps>(run_l1, red) : 0.0;
+        if (threadIdx.x == 0) {
+          atomicAdd(a.acc + part.img,
+                    static_cast<unsigned long long>(__double2ll_rn(s_ * kFixScale)));
+          if (l1)
+            atomicAdd(a.acc_l1 + part.img,
+                      static_cast<unsigned long long>(__double2ll_rn(s1 * kFixScaleL1)));
+        }
       }
+      __syncthreads();  // the moment rows are consumed before the next step overwrites them
+      slot ^= kSStep;
     }
-    __syncthreads();  // the moment rows are consumed before the next step overwrites them
-    cur = nxt;
+    if (failed) break;
+    part = nextp;
   }
 
   if (!a.reduce) return;
@@ -690,35 +690,25 @@ __global__ void __launch_bounds__(kSThreads, (SBwdConfig<HALO, TIn, TP>::kMinBlo
     fence_mbar_init();
   }
   __syncthreads();
-  SStep<HALO> cur = sfirst_step<HALO>(beg, end, g);
+  SPart part = sfirst_part(beg, end, g);
   if (tma && threadIdx.x < 3) prefetch_tensormap(a.tmap + threadIdx.x);
   grid_dependency_wait();
   grid_launch_dependents();
-  auto stage_step = [&](const SStep<HALO>& st) {
+  auto stage_rows = [&](const SStage& st) {
     if (tma) {
-      if (warp == 0) sstage_tma<TP, 3, HALO>(stg, a.tmap, st, &bar);
+      if (warp == 0) sstage_tma<TP, 3>(stg, a.tmap, st, &bar);
     } else {
       Step<HALO> s{};
       s.plane = st.plane;
       s.strip = st.strip;
       s.first = false;
-      s.t = st.h0() - HALO;
-      s.n = st.nh();
+      s.t = st.h0 - HALO;
+      s.n = st.nh;
       stage<TP, 3, SROWS, Step<HALO>, kSThreads>(stg + st.slot * SP, src, g, s, a.aligned16);
     }
   };
-  if (cur.live) stage_step(cur);
   unsigned phase = 0;
-  float2 wA[W2];  // the column's last 2*HALO rows of filtered (dm_dmu1, dm_dsigma1_sq)
-  float wB[W2];   // ... and of filtered dm_dsigma12
-#pragma unroll
-  for (int j = 0; j < W2; ++j) {
-    wA[j] = make_float2(0.f, 0.f);
-    wB[j] = 0.f;
-  }
-  const int W = static_cast<int>(g.W);
-
-  while (cur.live) {
+  auto wait_staged = [&]() -> bool {
     bool timed_out = false;
     if (tma) {
       timed_out = !mbar_wait_bounded(&bar, phase, a.wait_limit);
@@ -729,45 +719,79 @@ __global__ void __launch_bounds__(kSThreads, (SBwdConfig<HALO, TIn, TP>::kMinBlo
     if (__syncthreads_or(timed_out)) {
       if (threadIdx.x == 0) atomicOr(&g_device_error, kErrStagingTimeout);
       mbar_wait_bounded(&bar, phase ^ 1u, kWaitLimit);
-      return;
+      return false;
     }
-    const SStep<HALO> nxt = snext_step<HALO>(cur, g);
-    const bool early = nxt.live && !cur.pre && !nxt.pre;
-    if (early) stage_step(nxt);
-    // the epilogue's image values, loaded before the horizontal pass so they are in flight
-    const int gx = cur.strip * kStrip + c;
-    const bool in_x = gx < W;
-    const int64_t plane_off = static_cast<int64_t>(cur.plane) * g.HW;
-    const int off0 = cur.t * W + gx;
-    float xin[kSStep], yin[kSStep];
-    if (!cur.pre) {
-      const TIn* x_pl = img1 + plane_off;
-      const TIn* y_pl = img2 + plane_off;
-#pragma unroll
-      for (int k = 0; k < kSStep; ++k) {
-        const bool ld = in_x && k < cur.n;
-        xin[k] = ld ? ldg1(x_pl + off0 + k * W) : 0.f;
-        yin[k] = ld ? ldg1(y_pl + off0 + k * W) : 0.f;
-      }
-    }
-    sbwd_hpass<HALO, TIn, TP>(stg + cur.slot * SP, ring, cur.nh(), T);
-    __syncthreads();
-    if (nxt.live && !early) stage_step(nxt);
+    return true;
+  };
+  if (part.live) stage_rows({part.plane, part.strip, part.t0 - HALO, W2, 0});
+  const int W = static_cast<int>(g.W);
+  const float* col = ring + c;
 
-    const float* col = ring + c;
-    if (cur.pre) {
+  while (part.live) {
+    const SPart nextp = snext_part(part, g);
+    const int gx = part.strip * kStrip + c;
+    const bool in_x = gx < W;
+    const bool strip_full = part.strip * kStrip + kStrip <= W;
+    const int64_t plane_off = static_cast<int64_t>(part.plane) * g.HW + gx;
+    const TIn* x_pl = img1 + plane_off;
+    const TIn* y_pl = img2 + plane_off;
+    float chain = a.chain_scale;
+    float l1c = a.l1_scale;
+    if (a.grad_out) {
+      const float up = a.grad_out[a.grad_per_image ? part.img : 0];
+      chain = __fmul_rn(chain, up);
+      l1c = __fmul_rn(l1c, up);
+    }
+
+    // ---- preload ----
+    if (!wait_staged()) return;
+    sbwd_hpass<HALO, TIn, TP>(stg, ring, W2, T);
+    __syncthreads();
+    stage_rows({part.plane, part.strip, part.t0 + HALO, min(kSStep, part.t1 - part.t0), 0});
+    float2 wA[W2];  // the column's last 2*HALO rows of filtered (dm_dmu1, dm_dsigma1_sq)
+    float wB[W2];   // ... and of filtered dm_dsigma12
 #pragma unroll
-      for (int j = 0; j < W2; ++j) {
-        wA[j] = make_float2(col[j * RP + 0 * kStrip], col[j * RP + 1 * kStrip]);
-        wB[j] = col[j * RP + 2 * kStrip];
+    for (int j = 0; j < W2; ++j) {
+      wA[j] = make_float2(col[j * RP + 0 * kStrip], col[j * RP + 1 * kStrip]);
+      wB[j] = col[j * RP + 2 * kStrip];
+    }
+    __syncthreads();
+
+    // ---- regular steps ----
+    int slot = 0;
+    for (int t = part.t0; t < part.t1; t += kSStep) {
+      const int n = min(kSStep, part.t1 - t);
+      const bool last = t + kSStep >= part.t1;
+      const bool full = n == kSStep && strip_full;
+      if (!wait_staged()) return;
+      if (!last) stage_rows({part.plane, part.strip, t + kSStep + HALO,
+                             min(kSStep, part.t1 - t - kSStep), slot ^ kSStep});
+      // the epilogue's image values, loaded before the horizontal pass so they are in flight
+      const int off0 = t * W;
+      float xin[kSStep], yin[kSStep];
+      if (full) {
+#pragma unroll
+        for (int k = 0; k < kSStep; ++k) {
+          xin[k] = ldg1(x_pl + off0 + k * W);
+          yin[k] = ldg1(y_pl + off0 + k * W);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < kSStep; ++k) {
+          const bool ld = in_x && k < n;
+          xin[k] = ld ? ldg1(x_pl + off0 + k * W) : 0.f;
+          yin[k] = ld ? ldg1(y_pl + off0 + k * W) : 0.f;
+        }
       }
-    } else {
-      const int n = cur.n;
+      sbwd_hpass<HALO, TIn, TP>(stg + slot * SP, ring, n, T);
+      __syncthreads();
+      if (last && nextp.live) stage_rows({nextp.plane, nextp.strip, nextp.t0 - HALO, W2, 0});
+
       float2 nA[kSStep];
       float nB[kSStep];
 #pragma unroll
       for (int r = 0; r < kSStep; ++r) {
-        if (r < n) {
+        if (full || r < n) {
           nA[r] = make_float2(col[r * RP + 0 * kStrip], col[r * RP + 1 * kStrip]);
           nB[r] = col[r * RP + 2 * kStrip];
         } else {
@@ -777,13 +801,6 @@ __global__ void __launch_bounds__(kSThreads, (SBwdConfig<HALO, TIn, TP>::kMinBlo
       }
       auto rowA = [&](int j) { return j < W2 ? wA[j] : nA[j - W2]; };
       auto rowB = [&](int j) { return j < W2 ? wB[j] : nB[j - W2]; };
-      float chain = a.chain_scale;
-      float l1c = a.l1_scale;
-      if (a.grad_out) {
-        const float up = a.grad_out[a.grad_per_image ? cur.img : 0];
-        chain = __fmul_rn(chain, up);
-        l1c = __fmul_rn(l1c, up);
-      }
       float gv[kSStep];
 #pragma unroll
       for (int k = 0; k < kSStep; ++k) {
@@ -802,14 +819,14 @@ __global__ void __launch_bounds__(kSThreads, (SBwdConfig<HALO, TIn, TP>::kMinBlo
         }
       }
       auto store_grad = [&](auto* base) {
-        auto* gp = base + plane_off;
-        if (n == kSStep && in_x) {
+        auto* gp = base + plane_off + off0;
+        if (full) {
 #pragma unroll
-          for (int k = 0; k < kSStep; ++k) store1(gp + off0 + k * W, gv[k]);
+          for (int k = 0; k < kSStep; ++k) store1(gp + k * W, gv[k]);
         } else if (in_x) {
 #pragma unroll
           for (int k = 0; k < kSStep; ++k)
-            if (k < n) store1(gp + off0 + k * W, gv[k]);
+            if (k < n) store1(gp + k * W, gv[k]);
         }
       };
       if (a.grad_dtype == 0)
@@ -818,21 +835,24 @@ __global__ void __launch_bounds__(kSThreads, (SBwdConfig<HALO, TIn, TP>::kMinBlo
         store_grad(static_cast<__half*>(a.grad));
       else
         store_grad(static_cast<__nv_bfloat16*>(a.grad));
-      float2 cA[W2];
-      float cB[W2];
+      {
+        float2 cA[W2];
+        float cB[W2];
 #pragma unroll
-      for (int j = 0; j < W2; ++j) {
-        cA[j] = rowA(j + kSStep);
-        cB[j] = rowB(j + kSStep);
-      }
+        for (int j = 0; j < W2; ++j) {
+          cA[j] = j + kSStep < W2 ? wA[j + kSStep] : nA[j + kSStep - W2];
+          cB[j] = j + kSStep < W2 ? wB[j + kSStep] : nB[j + kSStep - W2];
+        }
 #pragma unroll
-      for (int j = 0; j < W2; ++j) {
-        wA[j] = cA[j];
-        wB[j] = cB[j];
+        for (int j = 0; j < W2; ++j) {
+          wA[j] = cA[j];
+          wB[j] = cB[j];
+        }
       }
+      __syncthreads();
+      slot ^= kSStep;
     }
-    __syncthreads();
-    cur = nxt;
+    part = nextp;
   }
 }
 

@@ -84,13 +84,17 @@ int fssim_set_gather_timeout_us(long long us);
 
 /* Kernels of the fused loss path (fssim_forward, fssim_backward and the sharded forward).
  * Both families compute bitwise-identical per-pixel results (partials, gradients, maps):
- *  FSSIM_KERNELS_STREAM (default): 64-thread CTAs, one output column per thread, the
- *      vertical filter window carried in registers from step to step;
+ *  FSSIM_KERNELS_STREAM: 64-thread CTAs, one output column per thread, the vertical filter
+ *      window carried in registers from step to step;
  *  FSSIM_KERNELS_TILE: 128-thread CTAs computing 2-column x 4-row tiles, the vertical halo
- *      kept in shared memory (the kernels of the map entry points in section 1).
+ *      kept in shared memory (the kernels of the map entry points in section 1);
+ *  FSSIM_KERNELS_AUTO (default): per launch, the family measured faster on a B200 for its
+ *      size: the streaming kernels, except the tile kernels below 2^21 channel-pixels
+ *      (B*C*H*W) and the tile backward from 2^27 channel-pixels.
  * Process-wide; applies to launches made after the call (FSSIM_ERR_ARGUMENT otherwise). */
 #define FSSIM_KERNELS_STREAM 0
 #define FSSIM_KERNELS_TILE 1
+#define FSSIM_KERNELS_AUTO 2
 int fssim_set_loss_kernels(int family);
 
 /* Number of SMs the kernels' persistent grids leave unused (default 0), for callers that

@@ -21,7 +21,7 @@ from tests import refpath
 
 pytestmark = pytest.mark.gpu
 
-STREAM, TILE = 0, 1
+STREAM, TILE, AUTO = 0, 1, 2
 SHAPES = [(1, 2, 40, 45), (2, 1, 37, 19), (1, 3, 64, 67), (2, 3, 96, 256), (1, 1, 5, 7),
           (2, 3, 37, 64), (1, 1, 5, 8), (1, 2, 130, 200), (3, 3, 200, 130)]
 
@@ -30,7 +30,7 @@ SHAPES = [(1, 2, 40, 45), (2, 1, 37, 19), (1, 3, 64, 67), (2, 3, 96, 256), (1, 1
 def ext(device):
     e = _ensure_cuda_extension()
     yield e
-    e.set_loss_kernels(STREAM)
+    e.set_loss_kernels(AUTO)
 
 
 def _both(ext, fn, a, b):
@@ -38,7 +38,7 @@ def _both(ext, fn, a, b):
     for fam in (STREAM, TILE):
         ext.set_loss_kernels(fam)
         out.append(refpath.value_and_grad(fn, a, b))
-    ext.set_loss_kernels(STREAM)
+    ext.set_loss_kernels(AUTO)
     return out
 
 
@@ -105,7 +105,7 @@ def test_stream_matches_tile_partials_1080p(ext):
         out, partials, sums = ext.loss_forward(a, b, 11, 0.01**2, 0.03**2, False, False, True, 1,
                                                False, 1.0 / n)
         outs.append((out, partials, sums))
-    ext.set_loss_kernels(STREAM)
+    ext.set_loss_kernels(AUTO)
     assert torch.equal(outs[0][1], outs[1][1])
     assert abs(outs[0][0].item() - outs[1][0].item()) <= 1e-7
 
