@@ -55,12 +55,14 @@ BWD_BYTES_F32 = 12 + 8 + 4    # read 3 partials, img1, img2; write grad
 FWD_FLOPS = 2 * 5 * 2 * 11 + 3 + 30   # 5 moments x 2 passes x 11 MACs, 3 products, epilogue
 BWD_FLOPS = 2 * 3 * 2 * 11 + 6        # 3 partial maps x 2 passes x 11 MACs, combine + chain
 
-# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of each kernel on
-# the 1080p workload, from one ncu capture of this kernel version (ncu flushes L2 before each
-# captured launch, so these are cold-L2 figures).
-NCU_TRAFFIC_BYTES = {"fwd": 60.75e6 + 27.58e6, "bwd": 172.90e6 + 15.77e6}
-NCU_TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:ssim_ -s 6 -c 2 "
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the 1080p
+# workload's kernels (the column-streaming forward and backward), from one ncu capture of
+# this kernel version (ncu flushes L2 before each captured launch: cold-L2 figures).
+NCU_TRAFFIC_BYTES = {"fwd": 57.26e6 + 26.32e6, "bwd": 143.63e6 + 15.70e6}
+NCU_TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:loss_ -s 4 -c 2 "
                       "python bench.py --steps 50 --warmup 3 --skip-extras")
+KERNEL_NAMES = {"fwd": "loss_fwd_kernel (column-streaming forward)",
+                "bwd": "loss_bwd_kernel (column-streaming backward)"}
 
 
 def load_peaks():
@@ -244,6 +246,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
     ap.add_argument("--skip-extras", action="store_true", help="only the headline number")
+    ap.add_argument("--dtype", default="f32", choices=["f32", "f16"],
+                    help="f16: the headline step on the same images in FP16 under autocast")
+    ap.add_argument("--kernels", default="auto", choices=["auto", "stream", "tile"],
+                    help="kernel family of the fused loss (fssim_set_loss_kernels)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -267,24 +273,31 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
     ext = _ensure_cuda_extension()
+    ext.set_loss_kernels({"stream": 0, "tile": 1, "auto": 2}[args.kernels])
     peaks = load_peaks()
     warm = max(3, args.warmup)
     K = args.steps
 
     # 4 rotating pairs per rank, generated on the host from rank-specific seeds
     host = [synthetic.make_pair("rgb_1080p", seed=1000 * rank + k) for k in range(N_ROT)]
+    half = args.dtype == "f16"
+    if half:
+        # the same images in FP16 under autocast (headline number only)
+        host = [(a.half(), b.half()) for a, b in host]
+        args.skip_extras = True
     pairs = [(a.to(dev).requires_grad_(True), b.to(dev)) for a, b in host]
     cpx_rank = pairs[0][0].numel()
 
     def step(i):
         x, y = pairs[i % N_ROT]
+        with torch.autocast("cuda", enabled=half):
+            if world > 1:
+                v, work = fdist.fused_ssim_dp(x, y, async_op=True)
+            else:
+                v = fb.fused_ssim(x, y)
+        v.backward()
         if world > 1:
-            v, work = fdist.fused_ssim_dp(x, y, async_op=True)
-            v.backward()
             work.wait()
-        else:
-            v = fb.fused_ssim(x, y)
-            v.backward()
         x.grad = None
         return v
 
@@ -317,10 +330,15 @@ def main():
     value = world * cpx_rank / (ms * 1e-3) / 1e6
 
     extras = {}
-    if rank == 0 and not args.skip_extras:
-        extras = measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, ms)
     if not args.skip_extras:
-        # every rank takes part: the batch is sharded over the ranks
+        if rank == 0:
+            extras.update(measure_kernels(ext, pairs, dev, K, warm, peaks, ms))
+        if world > 1:
+            dist.barrier()
+        # every rank takes part in the end-to-end step and in the sharded batch
+        extras["e2e"] = measure_e2e(fb, fdist, host, dev, K, warm, world, max_over_ranks)
+        if world == 1:
+            extras.update(measure_single_gpu(fb, synthetic, pairs, dev, K, warm, ms))
         del pairs
         torch.cuda.empty_cache()
         extras["batch_2048"] = measure_batch_2048(fb, fdist, dev, world, rank, warm, peaks,
@@ -334,14 +352,16 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": "Mpix/s", "n_gpus": world, "steps": K,
         "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "1x3x1080x1920 fp32, padding same, window 11, train, fwd+bwd "
-                               "per GPU (public API fused_ssim + backward)",
+        "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
+        "config": {"workload": f"1x3x1080x1920 {'fp16 images under autocast' if half else 'fp32'}"
+                               ", padding same, window 11, train, fwd+bwd per GPU (public API "
+                               "fused_ssim + backward)",
                    "global_batch": world, "shape_per_gpu": list(SHAPE),
                    "parallelism": f"dp{world}" if world > 1 else "none",
                    "l2": "4 rotating input pairs per GPU (200 MB > 126 MB L2)",
                    "timing": "CUDA events around K back-to-back steps, launch queue primed "
                              "by a GPU sleep before the first event; max over ranks",
+                   "kernels": args.kernels,
                    "rgb_mpix_per_s": value / 3.0},
         "host_us_per_step": host_us,
         "gpu_launches": 2 * K + (K if world > 1 else 0),
@@ -351,7 +371,8 @@ def main():
     print(json.dumps(line), flush=True)
 
 
-def measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, step_ms):
+def measure_kernels(ext, pairs, dev, K, warm, peaks, step_ms):
+    """The forward and backward kernels timed alone on this GPU, and their rooflines."""
     out = {}
     C1, C2 = 0.01**2, 0.03**2
     n = pairs[0][0].numel()
@@ -398,7 +419,7 @@ def measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, step_ms
         roof = {"bound": "fp32", "achieved": d["tflops"], "peak": fp32_peak, "unit": "TFLOP/s",
                 "frac": d["tflops"] / fp32_peak}
     roof["traffic"] = NCU_TRAFFIC_BYTES[dom]
-    roof.update(kernel=f"ssim_{dom}_kernel", launch_us=d["us"], traffic_unit="bytes per launch",
+    roof.update(kernel=KERNEL_NAMES[dom], launch_us=d["us"], traffic_unit="bytes per launch",
                 traffic_source=NCU_TRAFFIC_SOURCE, algorithmic_bytes=d["bytes"],
                 peak_source=("hbm: MEASURED_PEAKS.json (measured)" if peaks["source"] == "measured"
                              else "hbm: fallback") + "; fp32: 148 SMs x 128 lanes x 2 x sm_max_mhz")
@@ -413,16 +434,22 @@ def measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, step_ms
                             "frac_api_step": t_step_roof * 1e3 / step_ms,
                             "bound": "hbm", "bytes_per_cpx": FWD_BYTES_F32 + BWD_BYTES_F32}
     del parts
+    return out
 
-    # e2e through the public API with host buffers
+
+def measure_e2e(fb, fdist, host, dev, K, warm, world, max_over_ranks):
+    """The step through the public API from host (pinned) buffers on every rank: H2D of the
+    rank's image pair, fwd+bwd (sharded over the ranks), D2H of the loss, every step."""
     pinned = [(a.pin_memory(), b.pin_memory()) for a, b in host]
     loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+    n = host[0][0].numel()
+    esize = host[0][0].element_size()
 
     def e2e(i):
         a_h, b_h = pinned[i % N_ROT]
         x = a_h.to(dev, non_blocking=True).requires_grad_(True)
         y = b_h.to(dev, non_blocking=True)
-        v = fb.fused_ssim(x, y)
+        v = fdist.fused_ssim_dp(x, y) if world > 1 else fb.fused_ssim(x, y)
         v.backward()
         loss_h.copy_(v.detach(), non_blocking=True)
 
@@ -430,9 +457,18 @@ def measure_extras(ext, fb, synthetic, pairs, host, dev, K, warm, peaks, step_ms
     for i in range(warm):
         e2e(i)
     torch.cuda.synchronize()
-    t_e = event_time(e2e, e_iters)
-    out["e2e"] = {"value": n / (t_e * 1e-3) / 1e6, "unit": "Mpix/s", "ms_per_step": t_e,
-                  "h2d_bytes_per_step": 2 * n * 4, "d2h_bytes_per_step": 4, "steps": e_iters}
+    if world > 1:
+        torch.distributed.barrier()
+    t_e = max_over_ranks(event_time(e2e, e_iters))
+    return {"value": world * n / (t_e * 1e-3) / 1e6, "unit": "Mpix/s", "ms_per_step": t_e,
+            "h2d_bytes_per_step": 2 * n * esize * world, "d2h_bytes_per_step": 4 * world,
+            "steps": e_iters, "n_gpus": world}
+
+
+def measure_single_gpu(fb, synthetic, pairs, dev, K, warm, step_ms):
+    """One-GPU legs: the fused 3DGS loss, FP16 against FP32, the CPU baseline."""
+    out = {}
+    n = pairs[0][0].numel()
 
     # The 3DGS photometric loss 0.8*L1 + 0.2*(1-SSIM) at 1080p: fused (one forward and one
     # backward kernel) against the same loss composed from fused_ssim and torch's L1.

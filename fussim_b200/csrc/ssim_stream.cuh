@@ -230,10 +230,6 @@ __device__ __forceinline__ float svsum1(const Taps2<HALO, HW_>& T, int k, RowF r
   return __fmaf_rn(row(k + HALO), T.w[HALO].x, acc);
 }
 
-struct PixelOut {
-  float v, pm, ps, pc;
-};
-
 // SSIM value and its three partials of two pixels from their four filtered moments (MERGED
 // form), each operand a pair of pixels (packed FP32, identical to the map kernels'
 // epilogue).
@@ -336,7 +332,9 @@ struct SFwdConfig {
   static constexpr size_t kRingBytes = static_cast<size_t>(kRingRows) * kRP * sizeof(float);
   static constexpr size_t kSmem = kStageBytes + kRingBytes + 128;
   static constexpr int kFit = static_cast<int>((228 * 1024) / (kSmem + 1024));
-  // 7 CTAs/SM: a register budget of 146 holds the window and the part's pointers unspilled
+  // 6 CTAs/SM: the register budget (168) holds the carried window, the horizontal pass's
+  // rows and the part's constants; 7 or 8 CTAs/SM with 144 or 128 registers spill and
+  // measured slower on a B200
   static constexpr int kMinBlocks = kFit >= 6 ? 6 : kFit;
 };
 
@@ -416,7 +414,7 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
   const float* col = ring + c;
 
   while (part.live) {
-    const SPart nextp = snext_part(part, g);
+    SPart nextp;  // set at the part's last step
     // ---- constants of the part ----
     const int sx0 = part.strip * kStrip;
     const int gx = sx0 + c;
@@ -424,11 +422,10 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
     const bool col_ok = in_x && (!a.valid || (gx >= HALO && gx < W - HALO));
     const bool strip_fast = !a.clamp && sx0 + kStrip <= W &&
                             (!a.valid || (sx0 >= HALO && sx0 + kStrip <= W - HALO));
-    const int64_t plane_off = static_cast<int64_t>(part.plane) * g.HW;
-    float* mapp = a.map ? a.map + plane_off + gx : nullptr;
-    TP* q0 = TRAIN ? static_cast<TP*>(a.p0) + plane_off + gx : nullptr;
-    TP* q1 = TRAIN ? static_cast<TP*>(a.p1) + plane_off + gx : nullptr;
-    TP* q2 = TRAIN ? static_cast<TP*>(a.p2) + plane_off + gx : nullptr;
+    // this thread's pixel of the part's first row, as an offset into the (B, C, H, W) outputs;
+    // the output pointers are formed at the stores, which keeps them out of the registers
+    // the step loop carries
+    const int64_t pix = static_cast<int64_t>(part.plane) * g.HW + gx;
     const int l1_cols = W - sx0;
     double run_sum = 0.0, run_l1 = 0.0;
 
@@ -473,7 +470,10 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
       }
       __syncthreads();
       // the next part's preload fills both slots once this step's rows are consumed
-      if (last && nextp.live) stage_rows({nextp.plane, nextp.strip, nextp.t0 - HALO, W2, 0});
+      if (last) {
+        nextp = snext_part(part, g);
+        if (nextp.live) stage_rows({nextp.plane, nextp.strip, nextp.t0 - HALO, W2, 0});
+      }
 
       float2 nP[kSStep], nQ[kSStep];
       const int off0 = t * W;  // 32-bit in-plane row offset (planes < 2^31 elements)
@@ -495,18 +495,18 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
                                                  make_float2(Q0.x, Q1.x), make_float2(Q0.y, Q1.y),
                                                  C1v, C2v);
           if (a.reduce) step_sum += o.v.x + o.v.y;
-          const int off = off0 + k * W;
-          if (mapp) {
-            mapp[off] = o.v.x;
-            mapp[off + W] = o.v.y;
+          const int64_t off = pix + off0 + k * W;
+          if (a.map) {
+            a.map[off] = o.v.x;
+            a.map[off + W] = o.v.y;
           }
           if (TRAIN) {
-            store1(q0 + off, o.pm.x);
-            store1(q0 + off + W, o.pm.y);
-            store1(q1 + off, o.ps.x);
-            store1(q1 + off + W, o.ps.y);
-            store1(q2 + off, o.pc.x);
-            store1(q2 + off + W, o.pc.y);
+            store1(static_cast<TP*>(a.p0) + off, o.pm.x);
+            store1(static_cast<TP*>(a.p0) + off + W, o.pm.y);
+            store1(static_cast<TP*>(a.p1) + off, o.ps.x);
+            store1(static_cast<TP*>(a.p1) + off + W, o.ps.y);
+            store1(static_cast<TP*>(a.p2) + off, o.pc.x);
+            store1(static_cast<TP*>(a.p2) + off + W, o.pc.y);
           }
         }
       } else {
@@ -526,29 +526,36 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
           rlo = max(0, HALO - t);
           rhi = min(n, H - HALO - t);
         }
-#pragma unroll
-        for (int k = 0; k < kSStep; ++k) {
-          if (k < n) {
-            const float2 P = svsum<HALO, HW_>(T, k, rowP);
-            const float2 Q = svsum<HALO, HW_>(T, k, rowQ);
-            // the packed epilogue on the pixel twice (its first half is the result), the
-            // same instructions as the fast path's
-            const PixelOut2 o2 = ssim_pixel2<TRAIN>(splat(P.x), splat(P.y), splat(Q.x),
-                                                    splat(Q.y), C1v, C2v);
-            PixelOut o{o2.v.x, o2.pm.x, o2.ps.x, o2.pc.x};
-            const bool ok = col_ok && k >= rlo && k < rhi;
-            if (a.reduce) step_sum += (ok ? ((a.clamp && o.v < 0.f) ? 0.f : o.v) : 0.f);
-            if (in_x) {
-              const int off = off0 + k * W;
-              if (mapp) mapp[off] = o.v;
-              if (TRAIN) {
-                const bool live = !a.mask_partials || (ok && (!a.clamp || o.v >= 0.f));
-                if (!live) o.pm = o.ps = o.pc = 0.f;
-                store1(q0 + off, o.pm);
-                store1(q1 + off, o.ps);
-                store1(q2 + off, o.pc);
-              }
+        // masked outputs, also two rows at a time; a row at or past n is computed from zero
+        // window rows and neither summed nor stored
+        auto masked = [&](float v, float pm, float ps, float pc, int k) {
+          const bool ok = col_ok && k >= rlo && k < rhi;
+          float contrib = 0.f;
+          if (a.reduce) contrib = ok ? ((a.clamp && v < 0.f) ? 0.f : v) : 0.f;
+          if (in_x && k < n) {
+            const int64_t off = pix + off0 + k * W;
+            if (a.map) a.map[off] = v;
+            if (TRAIN) {
+              const bool live = !a.mask_partials || (ok && (!a.clamp || v >= 0.f));
+              if (!live) pm = ps = pc = 0.f;
+              store1(static_cast<TP*>(a.p0) + off, pm);
+              store1(static_cast<TP*>(a.p1) + off, ps);
+              store1(static_cast<TP*>(a.p2) + off, pc);
             }
+          }
+          return contrib;
+        };
+#pragma unroll
+        for (int k = 0; k < kSStep; k += 2) {
+          if (k < n) {
+            const float2 P0 = svsum<HALO, HW_>(T, k, rowP), P1 = svsum<HALO, HW_>(T, k + 1, rowP);
+            const float2 Q0 = svsum<HALO, HW_>(T, k, rowQ), Q1 = svsum<HALO, HW_>(T, k + 1, rowQ);
+            const PixelOut2 o = ssim_pixel2<TRAIN>(make_float2(P0.x, P1.x), make_float2(P0.y, P1.y),
+                                                   make_float2(Q0.x, Q1.x), make_float2(Q0.y, Q1.y),
+                                                   C1v, C2v);
+            const float c0 = masked(o.v.x, o.pm.x, o.ps.x, o.pc.x, k);
+            const float c1 = masked(o.v.y, o.pm.y, o.ps.y, o.pc.y, k + 1);
+            step_sum += c0 + c1;
           }
         }
       }
