@@ -8,8 +8,8 @@
 // step ahead), but the vertical pass is organised differently:
 //
 //   * one output column per thread: a CTA of 64 threads (2 warps) covers one strip;
-//   * the horizontal pass of a step (16 rows) writes its moment rows to a shared buffer
-//     that holds only that step's rows;
+//   * a step is 8 output rows; its horizontal pass writes its moment rows to a shared
+//     buffer that holds only that step's rows;
 //   * each thread keeps the last 2*HALO moment rows of its column in registers from one
 //     step to the next (a sliding window), and reads each moment value from shared memory
 //     exactly once; the vertical halo is never stored, copied or recomputed within a run
@@ -23,7 +23,14 @@
 // the same code, and the vertical sum adds symmetric pairs (d = 1..HALO) then the centre,
 // so per-pixel results are bitwise identical to the map kernels'; two maps are carried per
 // packed FP32 pair ((mu_x, mu_y) and (E[x^2 + y^2], E[xy]) in the forward), which keeps the
-// packed instructions without pairing adjacent columns.
+// packed instructions without pairing adjacent columns, and the epilogue runs on pairs of
+// output rows.
+//
+// Loop structure: an outer loop over the CTA's parts (one per column run it touches, with
+// the part's constants computed once) and an inner loop over the part's steps. Staging is
+// double-buffered in two slots of 8 rows: a regular step's rows are staged into the free
+// slot while the previous step is processed; a preload (2*HALO rows, both slots) and the
+// step after it are staged once the previous step's horizontal pass has finished.
 #pragma once
 
 #include "ssim_kernels.cuh"

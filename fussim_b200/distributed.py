@@ -136,17 +136,22 @@ class _Done:
         return True
 
 
-def _local_forward(a, b, window_size, C1, C2, valid, train, scale):
-    """Local shard: (out = local_sum * scale, partials). Runs the fused CUDA kernel."""
+def _local_forward(a, b, window_size, C1, C2, valid, train, scale, clamp=False,
+                   per_image=False):
+    """Local shard: (out, partials). out = local_sum * scale (one value), or with
+    ``per_image`` the (B_r,) vector of per-image sums * scale. Runs the fused CUDA kernel;
+    ``clamp`` clamps the map at 0 before reducing (nonnegative_ssim)."""
     ext = F._ensure_cuda_extension()
-    out, partials, _ = ext.loss_forward(a, b, window_size, C1, C2, valid, False, train,
-                                        F._REDUCE_SCALAR, False, scale)
+    reduce = F._REDUCE_PER_IMAGE if per_image else F._REDUCE_SCALAR
+    out, partials, _ = ext.loss_forward(a, b, window_size, C1, C2, valid, clamp, train, reduce,
+                                        False, scale)
     return out, partials
 
 
-def _local_backward(grad_out, a, b, partials, window_size, scale, grad_dtype):
+def _local_backward(grad_out, a, b, partials, window_size, scale, grad_dtype, per_image=False):
     ext = F._ensure_cuda_extension()
-    return ext.loss_backward(grad_out, a, b, partials, window_size, False, scale, grad_dtype)
+    return ext.loss_backward(grad_out, a, b, partials, window_size, per_image, scale,
+                             grad_dtype)
 
 
 def _peer_forward(a, b, window_size, valid, train, scale, mb):
@@ -229,4 +234,100 @@ def fused_ssim_dp(img1, img2, padding="same", train=True, window_size=11, group=
     if async_op:
         return out, works[0]
     works[0].wait()
+    return out
+
+
+# ------------------------------------------------------------------------------------
+# pytorch-msssim form over a sharded batch
+# ------------------------------------------------------------------------------------
+
+def shard_sizes(local_batch: int, group=None) -> list:
+    """Every rank's batch size, in rank order (one all-gather per distinct local size,
+    cached)."""
+    key = ("B", local_batch, id(group))
+    if key not in _count_cache:
+        dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" \
+            else torch.device("cpu")
+        t = torch.tensor([local_batch], dtype=torch.int64, device=dev)
+        parts = [torch.empty_like(t) for _ in range(dist.get_world_size(group))]
+        dist.all_gather(parts, t, group=group)
+        _count_cache[key] = [int(x.item()) for x in parts]
+    return _count_cache[key]
+
+
+def _gather_per_image(local, sizes, group):
+    """Concatenation in rank order of every rank's (B_r,) vector (padded to the largest
+    shard for the all-gather, then trimmed)."""
+    width = max(sizes)
+    buf = local.new_zeros(width)
+    buf[:local.numel()] = local
+    parts = [torch.empty_like(buf) for _ in sizes]
+    dist.all_gather(parts, buf, group=group)
+    return torch.cat([p[:n] for p, n in zip(parts, sizes)])
+
+
+class _ShardedMsssim(torch.autograd.Function):
+    """Forward: the local fused kernel (clamp and per-image reduction in the kernel), then
+    the exchange (a sum for the global mean, an all-gather of the per-image vectors).
+    Backward: local; with per-image values the rank's slice of the upstream gradient."""
+
+    @staticmethod
+    def forward(ctx, img1, img2, C1, C2, window_size, clamp, per_image, half, scale, group):
+        a, b = F._kernel_inputs(img1, img2, half)
+        out, partials = _local_forward(a, b, window_size, C1, C2, True, True, scale, clamp,
+                                       per_image)
+        if per_image:
+            sizes = shard_sizes(a.shape[0], group)
+            rank = dist.get_rank(group)
+            ctx.lo, ctx.n = sum(sizes[:rank]), sizes[rank]
+            out = _gather_per_image(out, sizes, group)
+        else:
+            dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
+        ctx.save_for_backward(a, b, partials)
+        ctx.window_size = window_size
+        ctx.per_image = per_image
+        ctx.scale = scale if scale != float("inf") else 0.0
+        ctx.grad_dtype = F._DTYPE_CODE.get(img1.dtype, 0)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        a, b, partials = ctx.saved_tensors
+        if ctx.per_image:
+            grad_out = grad_out[ctx.lo:ctx.lo + ctx.n]
+        grad = _local_backward(grad_out, a, b, partials, ctx.window_size, ctx.scale,
+                               ctx.grad_dtype, ctx.per_image)
+        return (grad,) + (None,) * 9
+
+
+def ssim_dp(X, Y, data_range=255, size_average=True, win_size=11, win_sigma=1.5, win=None,
+            K=(0.01, 0.03), nonnegative_ssim=False, group=None):
+    """``fussim_b200.ssim`` (pytorch-msssim form, 'valid' padding) of the batch formed by
+    every rank's (X, Y) shard.
+
+    With ``size_average=True`` every rank gets the global mean over all shards' pixels (one
+    all-reduce of the shard sums); with ``size_average=False`` every rank gets the (B,)
+    vector of per-image values of the whole batch in rank order (one all-gather of the
+    per-image vectors), and the gradient reaching this rank's X is that of its own images'
+    entries. The argument checks and their messages are the reference's ``ssim``
+    (fussim/__init__.py:636-658). Every rank must make the same sequence of calls.
+    """
+    C1, C2 = F._msssim_constants(data_range, win_size, win_sigma, win, K)
+    half = torch.is_autocast_enabled()
+    if not half:
+        X, Y = F._float_path_inputs(X, Y)
+    per_image = not size_average
+    if per_image:
+        scale = F._inv(F._count(tuple(X.shape), win_size, True, True))
+    else:
+        scale = F._inv(global_count(F._count(tuple(X.shape), win_size, True, False), group))
+    if torch.is_grad_enabled() and X.requires_grad:
+        return _ShardedMsssim.apply(X, Y, C1, C2, win_size, bool(nonnegative_ssim), per_image,
+                                    half, scale, group)
+    a, b = F._kernel_inputs(X, Y, half)
+    out, _ = _local_forward(a, b, win_size, C1, C2, True, False, scale, bool(nonnegative_ssim),
+                            per_image)
+    if per_image:
+        return _gather_per_image(out, shard_sizes(a.shape[0], group), group)
+    dist.all_reduce(out, op=dist.ReduceOp.SUM, group=group)
     return out

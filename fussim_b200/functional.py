@@ -378,6 +378,18 @@ def ssim(
     Always 'valid' padding; ``size_average=False`` returns shape (B,); ``nonnegative_ssim``
     clamps the per-pixel map at 0 (the reference's semantics) before reducing.
     """
+    C1, C2 = _msssim_constants(data_range, win_size, win_sigma, win, K)
+    train = torch.is_grad_enabled() and X.requires_grad
+    half = torch.is_autocast_enabled()
+    if not half:
+        X, Y = _float_path_inputs(X, Y)
+    reduce = _REDUCE_SCALAR if size_average else _REDUCE_PER_IMAGE
+    return _reduce(X, Y, C1, C2, win_size, True, bool(nonnegative_ssim), reduce, train, half)
+
+
+def _msssim_constants(data_range, win_size, win_sigma, win, K):
+    """The pytorch-msssim argument checks of the reference's ``ssim`` (same messages, same
+    order: fussim/__init__.py:636-658); returns (C1, C2)."""
     if win_size not in SUPPORTED_WINDOW_SIZES:
         raise ValueError(
             f"win_size must be one of {SUPPORTED_WINDOW_SIZES}, got {win_size}. "
@@ -398,15 +410,7 @@ def ssim(
     K1, K2 = K
     if not (0 < K1 < 1 and 0 < K2 < 1):
         raise ValueError(f"K values must be in (0, 1), got K1={K1}, K2={K2}")
-
-    C1 = (K1 * data_range) ** 2
-    C2 = (K2 * data_range) ** 2
-    train = torch.is_grad_enabled() and X.requires_grad
-    half = torch.is_autocast_enabled()
-    if not half:
-        X, Y = _float_path_inputs(X, Y)
-    reduce = _REDUCE_SCALAR if size_average else _REDUCE_PER_IMAGE
-    return _reduce(X, Y, C1, C2, win_size, True, bool(nonnegative_ssim), reduce, train, half)
+    return (K1 * data_range) ** 2, (K2 * data_range) ** 2
 
 
 class SSIM(torch.nn.Module):

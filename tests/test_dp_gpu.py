@@ -5,7 +5,9 @@ of a seeded global batch; the value of fused_ssim_dp must equal fused_ssim of th
 batch on one GPU, and each rank's gradient the matching slice of its gradient. NVLink
 SHARP reductions are switched off (NCCL_NVLS_ENABLE=0). The shard sums travel through the
 peer mailboxes (CUDA IPC over NVLink); NCCL carries only the one-time set-up (the pixel
-count and the exchange of the IPC handles).
+count and the exchange of the IPC handles). ``ssim_dp(size_average=False)`` must give every
+rank the whole batch's per-image vector of ``ssim`` and each rank the slice of the gradient
+of a per-image weighted loss.
 """
 
 import datetime
@@ -20,6 +22,7 @@ pytestmark = pytest.mark.gpu
 
 SHARDS = (1, 2)
 SHAPE = (3, 96, 200)
+WEIGHTS = (1.0, -2.0, 0.5)   # per-image weights of the ssim_dp loss
 
 
 def _free_port():
@@ -60,6 +63,12 @@ def _worker(rank, port, queue):
             out[padding] = (float(v.detach()), a.grad.cpu().numpy().copy())
         # the peer path (mailboxes over CUDA IPC) must have been used, not a collective
         out["peer"] = len(D._mailboxes) == 1
+        # pytorch-msssim form over NCCL: per-image vector of the whole batch on every rank
+        a = a_all[lo:lo + SHARDS[rank]].to(dev).requires_grad_(True)
+        b = b_all[lo:lo + SHARDS[rank]].to(dev)
+        v = D.ssim_dp(a, b, data_range=1.0, size_average=False)
+        (v * torch.tensor(WEIGHTS, device=dev)).sum().backward()
+        out["per_image"] = (v.detach().cpu().numpy().copy(), a.grad.cpu().numpy().copy())
         D.release_mailboxes()
         queue.put((rank, out))
     finally:
@@ -94,3 +103,13 @@ def test_dp_two_gpus_matches_single_gpu():
             lo = sum(SHARDS[:rank])
             ref = g[lo:lo + SHARDS[rank]]
             assert (torch.from_numpy(grad) - ref).abs().max().item() <= 1e-5 * ref.abs().max().item()
+    x = a_all.cuda().requires_grad_(True)
+    v = fb.ssim(x, b_all.cuda(), data_range=1.0, size_average=False)
+    (v * torch.tensor(WEIGHTS, device=v.device)).sum().backward()
+    g = x.grad.cpu()
+    for rank in range(2):
+        vals, grad = res[rank]["per_image"]
+        assert (torch.from_numpy(vals) - v.detach().cpu()).abs().max().item() <= 1e-6
+        lo = sum(SHARDS[:rank])
+        ref = g[lo:lo + SHARDS[rank]]
+        assert (torch.from_numpy(grad) - ref).abs().max().item() <= 1e-5 * ref.abs().max().item()
