@@ -456,7 +456,8 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
       wP[j] = make_float2(col[j * RP + 0 * kStrip], col[j * RP + 2 * kStrip]);
       wQ[j] = make_float2(col[j * RP + 1 * kStrip], col[j * RP + 3 * kStrip]);
     }
-    __syncthreads();
+    // (no barrier here: the step's staging wait is a barrier of the whole CTA, and it comes
+    // before the next horizontal pass overwrites the moment rows just read)
 
     // ---- regular steps: output rows [t, t + n) ----
     int slot = 0;
@@ -594,7 +595,8 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
                       static_cast<unsigned long long>(__double2ll_rn(s1 * kFixScaleL1)));
         }
       }
-      __syncthreads();  // the moment rows are consumed before the next step overwrites them
+      // the moment rows of this step were read into registers before the epilogue; the next
+      // step's staging wait (a CTA barrier) orders those reads before its horizontal pass
       slot ^= kSStep;
     }
     if (failed) break;
@@ -769,7 +771,7 @@ __global__ void __launch_bounds__(kSThreads, (SBwdConfig<HALO, TIn, TP>::kMinBlo
       wA[j] = make_float2(col[j * RP + 0 * kStrip], col[j * RP + 1 * kStrip]);
       wB[j] = col[j * RP + 2 * kStrip];
     }
-    __syncthreads();
+    // (no barrier: the staging wait of the first step orders these reads before its pass)
 
     // ---- regular steps ----
     int slot = 0;
@@ -863,7 +865,8 @@ __global__ void __launch_bounds__(kSThreads, (SBwdConfig<HALO, TIn, TP>::kMinBlo
           wB[j] = cB[j];
         }
       }
-      __syncthreads();
+      // the next step's staging wait (a CTA barrier) orders this step's reads of the filtered
+      // rows before the next horizontal pass overwrites them
       slot ^= kSStep;
     }
     part = nextp;
