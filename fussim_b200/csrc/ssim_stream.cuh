@@ -339,10 +339,12 @@ struct SFwdConfig {
   static constexpr size_t kRingBytes = static_cast<size_t>(kRingRows) * kRP * sizeof(float);
   static constexpr size_t kSmem = kStageBytes + kRingBytes + 128;
   static constexpr int kFit = static_cast<int>((228 * 1024) / (kSmem + 1024));
-  // 6 CTAs/SM: the register budget (168) holds the carried window, the horizontal pass's
-  // rows and the part's constants; 7 or 8 CTAs/SM with 144 or 128 registers spill and
-  // measured slower on a B200
-  static constexpr int kMinBlocks = kFit >= 6 ? 6 : kFit;
+  // Launch bound of 5 CTAs/SM (a register target of 204): every instantiation compiles to
+  // at most 168 registers, so 6 CTAs/SM still fit (shared memory allows more), and on a
+  // B200 this code ran 2-3 % faster than the same kernels built for a bound of 6 (also 168
+  // registers). 7 or 8 CTAs/SM (144 or 128 registers) spill and ran slower; 4 (232
+  // registers) ran slower too.
+  static constexpr int kMinBlocks = kFit >= 5 ? 5 : kFit;
 };
 
 template <int HALO, typename TIn, typename TP, bool TRAIN>
