@@ -58,7 +58,7 @@ BWD_FLOPS = 2 * 3 * 2 * 11 + 6        # 3 partial maps x 2 passes x 11 MACs, com
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the 1080p
 # workload's kernels (the column-streaming forward and backward), from one ncu capture of
 # this kernel version (ncu flushes L2 before each captured launch: cold-L2 figures).
-NCU_TRAFFIC_BYTES = {"fwd": 57.26e6 + 26.32e6, "bwd": 143.63e6 + 15.70e6}
+NCU_TRAFFIC_BYTES = {"fwd": 57.51e6 + 26.33e6, "bwd": 143.76e6 + 13.24e6}
 NCU_TRAFFIC_SOURCE = ("ncu --set full --clock-control none -k regex:loss_ -s 4 -c 2 "
                       "python bench.py --steps 50 --warmup 3 --skip-extras")
 KERNEL_NAMES = {"fwd": "loss_fwd_kernel (column-streaming forward)",
