@@ -386,7 +386,8 @@ struct FusedLossFn : public torch::autograd::Function<FusedLossFn> {
                                torch::Tensor img2, double C1, double C2, int64_t window_size,
                                bool valid, bool clamp, int64_t reduce, bool half,
                                double scale, double chain_scale, double l1_weight,
-                               double out_offset, double l1_scale, const fssim_dp_args* dp) {
+                               double out_offset, double l1_scale, const fssim_dp_args* dp,
+                               bool gather) {
     torch::Tensor a, b;
     if (half) {
       a = img1.scalar_type() == at::kHalf ? img1 : img1.to(at::kHalf);
@@ -398,7 +399,7 @@ struct FusedLossFn : public torch::autograd::Function<FusedLossFn> {
     auto r = loss_forward_impl(a, b, static_cast<int>(window_size), C1, C2, valid, clamp, true,
                                static_cast<int>(reduce), false, scale, l1_weight, out_offset,
                                dp, /*with_sums=*/false);
-    if (dp) {
+    if (dp && gather) {
       // sharded loss: out = scale * (sum over every rank's shard), formed on this GPU
       check_status(fssim_dp_gather(dp, static_cast<float>(scale),
                                    std::get<0>(r).data_ptr<float>(), current_stream()));
@@ -421,7 +422,7 @@ struct FusedLossFn : public torch::autograd::Function<FusedLossFn> {
                                    ctx->saved_data["chain"].toDouble(),
                                    static_cast<int>(ctx->saved_data["gdt"].toInt()),
                                    ctx->saved_data["l1"].toDouble());
-    torch::autograd::variable_list out(15);
+    torch::autograd::variable_list out(16);
     out[0] = grad;
     return out;
   }
@@ -435,19 +436,21 @@ torch::Tensor fused_loss(torch::Tensor img1, torch::Tensor img2, double C1, doub
                          double l1_scale) {
   return FusedLossFn::apply(img1, img2, C1, C2, window_size, valid, clamp, reduce, half, scale,
                             chain_scale, l1_weight, out_offset, l1_scale,
-                            static_cast<const fssim_dp_args*>(nullptr));
+                            static_cast<const fssim_dp_args*>(nullptr), false);
 }
 
 // The fused loss of this rank's shard of a batch sharded over several GPUs: the value is
 // the mean over every rank's shard (peer mailboxes, fssim_forward_dp + fssim_dp_gather),
-// the gradient is local (d(out)/d(map) = scale = 1 / global count).
+// the gradient is local (d(out)/d(map) = scale = 1 / global count). With gather = false the
+// forward only publishes this rank's sum; the caller runs dp_gather on `out` itself (on
+// another stream, so that the backward does not wait for the other ranks).
 torch::Tensor fused_loss_dp(torch::Tensor img1, torch::Tensor img2, int64_t window_size,
                             bool valid, bool half, double scale, double chain_scale,
                             int64_t world, int64_t rank, int64_t seq,
-                            std::vector<int64_t> mailboxes) {
+                            std::vector<int64_t> mailboxes, bool gather) {
   const fssim_dp_args d = make_dp(world, rank, seq, mailboxes);
   return FusedLossFn::apply(img1, img2, 0.01 * 0.01, 0.03 * 0.03, window_size, valid, false,
-                            int64_t{1}, half, scale, chain_scale, 0.0, 0.0, 0.0, &d);
+                            int64_t{1}, half, scale, chain_scale, 0.0, 0.0, 0.0, &d, gather);
 }
 
 }  // namespace
@@ -464,7 +467,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_scale"), py::arg("l1_weight") = 0.0, py::arg("out_offset") = 0.0);
   m.def("loss_backward", &loss_backward);
   m.def("fused_loss", &fused_loss);
-  m.def("fused_loss_dp", &fused_loss_dp);
+  m.def("fused_loss_dp", &fused_loss_dp, py::arg("img1"), py::arg("img2"),
+        py::arg("window_size"), py::arg("valid"), py::arg("half"), py::arg("scale"),
+        py::arg("chain_scale"), py::arg("world"), py::arg("rank"), py::arg("seq"),
+        py::arg("mailboxes"), py::arg("gather") = true);
   m.def("loss_forward_dp", &loss_forward_dp);
   m.def("dp_gather", &dp_gather);
   m.def("dp_mailbox_alloc", &dp_mailbox_alloc);

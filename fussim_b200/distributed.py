@@ -72,10 +72,16 @@ class _Mailboxes:
             self.ptrs = [self.local if r == self.rank else ext.ipc_open_handle(h)
                          for r, h in enumerate(handles)]
         self.seq = 0
+        # the deferred gather of an asynchronous step (a _LazyGather), launched by its wait()
+        # or before this rank's next sharded forward: a rank publishes step k+1 only after
+        # its own gather of step k, which keeps every peer within the two slot sets
+        self.pending = None
         dist.barrier(group=group)  # every rank has mapped every mailbox before step 1
 
     def release(self):
         ext = F._ensure_cuda_extension()
+        if self.pending is not None:
+            self.pending.wait()
         for r, p in enumerate(self.ptrs):
             if r != self.rank:
                 ext.ipc_close_handle(p)
@@ -136,6 +142,33 @@ class _Done:
         return True
 
 
+class _LazyGather:
+    """Handle of a peer exchange whose gather kernel is not launched yet.
+
+    ``wait()`` launches it on the current stream, after whatever the caller queued since the
+    forward (typically the backward, which then does not wait for the other ranks'
+    forwards); the next sharded forward of the same group launches it first if ``wait()``
+    was not called. No host synchronisation either way."""
+
+    def __init__(self, mb, out, scale, seq):
+        self._mb = mb
+        self._args = (out, scale, seq)
+        mb.pending = self
+
+    def wait(self):
+        if self._args is not None:
+            out, scale, seq = self._args
+            self._args = None
+            mb = self._mb
+            if mb.pending is self:
+                mb.pending = None
+            F._ensure_cuda_extension().dp_gather(out, scale, mb.world, mb.rank, seq, mb.ptrs)
+        return True
+
+    def is_completed(self):
+        return self._args is None
+
+
 def _local_forward(a, b, window_size, C1, C2, valid, train, scale, clamp=False,
                    per_image=False):
     """Local shard: (out, partials). out = local_sum * scale (one value), or with
@@ -157,6 +190,8 @@ def _local_backward(grad_out, a, b, partials, window_size, scale, grad_dtype, pe
 def _peer_forward(a, b, window_size, valid, train, scale, mb):
     """Local shard forward that publishes its sum, then the gather: out = global mean."""
     ext = F._ensure_cuda_extension()
+    if mb.pending is not None:
+        mb.pending.wait()
     mb.seq += 1
     out, partials = ext.loss_forward_dp(a, b, window_size, 0.01**2, 0.03**2, valid, train,
                                         scale, mb.world, mb.rank, mb.seq, mb.ptrs)
@@ -202,8 +237,9 @@ def fused_ssim_dp(img1, img2, padding="same", train=True, window_size=11, group=
     ``fused_ssim`` of the concatenation of all shards. With ``async_op=True`` the call
     returns ``(value, work)`` without waiting for the exchange: the local backward can run
     meanwhile, and ``work.wait()`` must be called before the value is read. (On the peer
-    path the exchange is already ordered on the current stream and ``wait`` returns at
-    once.) Every rank must make the same sequence of calls.
+    path ``wait`` launches the gather of the shard sums on the current stream, after the
+    backward, so the backward does not wait for the other ranks; there is no host
+    synchronisation.) Every rank must make the same sequence of calls.
     """
     if padding not in F.ALLOWED_PADDING:
         raise ValueError(f"padding must be one of {F.ALLOWED_PADDING}, but got '{padding}'")
@@ -218,14 +254,18 @@ def fused_ssim_dp(img1, img2, padding="same", train=True, window_size=11, group=
     works: list = []
     mb = _mailboxes_for(group, img1.device) if (train and img1.is_cuda) else None
     if mb is not None:
-        # peer path: the C++ autograd function of the extension (forward publishes and
-        # gathers the shard sums, backward is local)
+        # peer path: the C++ autograd function of the extension (forward publishes the shard
+        # sum, backward is local); the gather of the shard sums follows on this stream, or,
+        # with async_op, on the mailboxes' stream so that the backward need not wait for the
+        # other ranks' forwards
         ext = F._ensure_cuda_extension()
+        if mb.pending is not None:
+            mb.pending.wait()
         mb.seq += 1
-        out = ext.fused_loss_dp(img1, img2, window_size, valid, half, scale,
-                                scale if scale != float("inf") else 0.0, mb.world, mb.rank,
-                                mb.seq, mb.ptrs)
-        works.append(_Done())
+        chain = scale if scale != float("inf") else 0.0
+        out = ext.fused_loss_dp(img1, img2, window_size, valid, half, scale, chain, mb.world,
+                                mb.rank, mb.seq, mb.ptrs, gather=not async_op)
+        works.append(_LazyGather(mb, out, scale, mb.seq) if async_op else _Done())
     elif train:
         out = _ShardedSSIM.apply(img1, img2, window_size, valid, half, scale, group, works)
     else:

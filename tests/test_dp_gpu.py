@@ -54,13 +54,24 @@ def _worker(rank, port, queue):
         lo = sum(SHARDS[:rank])
         out = {}
         for padding in ("same", "valid"):
-            a = a_all[lo:lo + SHARDS[rank]].to(dev).requires_grad_(True)
-            b = b_all[lo:lo + SHARDS[rank]].to(dev)
-            v, work = D.fused_ssim_dp(a, b, padding=padding, async_op=True)
-            v.backward()
-            work.wait()
+            # several steps, asynchronous (gather on a side stream) and synchronous mixed:
+            # every one must give the same value and gradient
+            vals, grads = [], []
+            for it in range(5):
+                a = a_all[lo:lo + SHARDS[rank]].to(dev).requires_grad_(True)
+                b = b_all[lo:lo + SHARDS[rank]].to(dev)
+                if it % 2 == 0:
+                    v, work = D.fused_ssim_dp(a, b, padding=padding, async_op=True)
+                    v.backward()
+                    work.wait()
+                else:
+                    v = D.fused_ssim_dp(a, b, padding=padding)
+                    v.backward()
+                vals.append(v.detach().clone())
+                grads.append(a.grad)
             torch.cuda.synchronize()
-            out[padding] = (float(v.detach()), a.grad.cpu().numpy().copy())
+            assert all(torch.equal(g, grads[0]) for g in grads)
+            out[padding] = ([float(x) for x in vals], a.grad.cpu().numpy().copy())
         # the peer path (mailboxes over CUDA IPC) must have been used, not a collective
         out["peer"] = len(D._mailboxes) == 1
         # pytorch-msssim form over NCCL: per-image vector of the whole batch on every rank
@@ -98,8 +109,8 @@ def test_dp_two_gpus_matches_single_gpu():
         v.backward()
         g = x.grad.cpu()
         for rank in range(2):
-            val, grad = res[rank][padding]
-            assert abs(val - v.item()) <= 1e-6
+            vals, grad = res[rank][padding]
+            assert all(abs(val - v.item()) <= 1e-6 for val in vals)
             lo = sum(SHARDS[:rank])
             ref = g[lo:lo + SHARDS[rank]]
             assert (torch.from_numpy(grad) - ref).abs().max().item() <= 1e-5 * ref.abs().max().item()

@@ -5,8 +5,10 @@ points next to their single-GPU counterparts on the same inputs:
 
 * ``fused_ssim_dp`` goes through the peer mailboxes (the Python set-up of
   ``fussim_b200.distributed``: the same-host check, the IPC handle exchange, the published
-  sum and the gather kernel); its value must equal ``fused_ssim`` to FP32 rounding of the
-  final scale and its gradient bitwise;
+  sum and the gather kernel, launched by the forward or, with ``async_op``, by ``wait()``
+  after the backward or by the next step's call);
+  its value must equal ``fused_ssim`` to FP32 rounding of the final scale and its gradient
+  bitwise;
 * ``ssim_dp`` goes through NCCL collectives (an all-reduce of the shard sum, or an
   all-gather of the per-image vector); value and gradient must equal ``ssim`` bitwise,
   with the clamp of ``nonnegative_ssim`` and per-image weights in the loss.
@@ -66,15 +68,25 @@ def _run(res, dev, fb, D, synthetic):
     a, b = synthetic.pair_noise(SHAPE, 0.1, seed=41)
     a, b = a.to(dev), b.to(dev)
     for padding in ("same", "valid"):
-        x = a.clone().requires_grad_(True)
-        v = D.fused_ssim_dp(x, b, padding=padding)
-        v.backward()
-        y = a.clone().requires_grad_(True)
-        r = fb.fused_ssim(y, b, padding=padding)
-        r.backward()
-        torch.cuda.synchronize()
-        res[("fused", padding)] = (v.item(), r.item(),
-                                   bool(torch.equal(x.grad, y.grad)))
+        for async_op in (False, True):
+            # three steps in a row: with async_op the gather is launched by wait() (last
+            # step) or by the next step's call (earlier steps)
+            for it in range(3):
+                x = a.clone().requires_grad_(True)
+                if async_op:
+                    v, work = D.fused_ssim_dp(x, b, padding=padding, async_op=True)
+                    v.backward()
+                    if it == 2:
+                        work.wait()
+                else:
+                    v = D.fused_ssim_dp(x, b, padding=padding)
+                    v.backward()
+            y = a.clone().requires_grad_(True)
+            r = fb.fused_ssim(y, b, padding=padding)
+            r.backward()
+            torch.cuda.synchronize()
+            res[("fused", padding, async_op)] = (v.item(), r.item(),
+                                                 bool(torch.equal(x.grad, y.grad)))
     b2 = (1.0 - b) * 0.5 + 0.5 * a    # partly anti-correlated: the clamp is exercised
     w = torch.tensor(WEIGHTS, device=dev)
     for size_average, nonneg in MSSSIM_CASES:
@@ -111,8 +123,9 @@ def one_rank():
 
 
 @pytest.mark.parametrize("padding", ["same", "valid"])
-def test_fused_ssim_dp_one_rank_matches_fused_ssim(one_rank, padding):
-    v, r, grads_equal = one_rank[("fused", padding)]
+@pytest.mark.parametrize("async_op", [False, True])
+def test_fused_ssim_dp_one_rank_matches_fused_ssim(one_rank, padding, async_op):
+    v, r, grads_equal = one_rank[("fused", padding, async_op)]
     assert abs(v - r) <= 1e-7
     assert grads_equal
 
