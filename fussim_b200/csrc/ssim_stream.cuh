@@ -65,11 +65,13 @@ __device__ __forceinline__ double block_sum_w(double v, double* red) {
 }
 
 // Start of CTA b's range of strip-rows for the streaming kernels: as cta_range_start, with a
-// run part costing its rows plus the 2*HALO rows of its preload.
+// run part costing its rows plus 2*HALO + 4 rows for its preload (the preload's rows, its
+// exposed staging wait and the part's set-up; 2*HALO alone, and 2*HALO + 8, balanced the
+// grid slightly worse on a B200).
 template <int HALO>
 __device__ __forceinline__ int64_t scta_range_start(const Geometry& g, int64_t b, int64_t G) {
   const int64_t runs = g.LT / g.H;
-  const int64_t per = g.H + 2 * HALO;
+  const int64_t per = g.H + 2 * HALO + 4;
   const int64_t A = (runs * per * b) / G;
   const int64_t r = A / per;
   const int64_t o = A - r * per;
