@@ -227,6 +227,15 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+// L2 prefetch of one tensor-map box (no shared memory, no completion to wait for). L2 is
+// the point of coherence of global memory, so a prefetch issued while an earlier kernel may
+// still write the same lines cannot make a later load read stale data.
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];\n" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
 // One 3-D tiled bulk copy global -> shared (coordinates: column, row, plane).
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y,
                                             int z, uint64_t* bar) {

@@ -104,6 +104,19 @@ __device__ __forceinline__ SPart sfirst_part(int64_t beg, int64_t end, const Geo
   return p;
 }
 
+// L2 prefetch of the TMA boxes of a part's preload (rows [t0 - HALO, t0 + HALO)), issued
+// before the wait for the previous kernel: thread m * 2 + b (m < NMAP, b < 2) prefetches
+// box b of map m. A hint: rows are clamped to the image.
+template <int HALO, int NMAP>
+__device__ __forceinline__ void prefetch_preload(const CUtensorMap* maps, const SPart& p,
+                                                 const Geometry& g) {
+  const int i = threadIdx.x;
+  if (!p.live || i >= 2 * NMAP) return;
+  const int y = p.t0 - HALO + (i & 1) * kSStep;
+  tma_prefetch_3d(maps + (i >> 1), max(p.strip * kStrip - kLeft, 0),
+                  min(max(y, 0), static_cast<int>(g.H) - 1), p.plane);
+}
+
 __device__ __forceinline__ SPart snext_part(const SPart& c, const Geometry& g) {
   SPart p = c;
   if (!c.live || c.rest == 0) {
@@ -383,6 +396,12 @@ __global__ void __launch_bounds__(kSThreads, (SFwdConfig<HALO, TIn, TP, TRAIN>::
   __syncthreads();
   SPart part = sfirst_part(beg, end, g);
   if (tma && threadIdx.x < 2) prefetch_tensormap(a.tmap + threadIdx.x);
+  // the first preload's boxes into L2 while the previous kernel finishes (not in the FP32
+  // 11-tap forward: there the extra code made ptxas spill 12 bytes in the step loop, which
+  // cost 3 % on large batches, more than the prefetch saves at 1080p)
+  if constexpr (!(sizeof(TIn) == 4 && HALO == 5)) {
+    if (tma) prefetch_preload<HALO, 2>(a.tmap, part, g);
+  }
   grid_dependency_wait();
   grid_launch_dependents();
   // staging of rows: TMA boxes issued by warp 0, or cp.async by the whole CTA
@@ -712,6 +731,8 @@ __global__ void __launch_bounds__(kSThreads, (SBwdConfig<HALO, TIn, TP>::kMinBlo
   __syncthreads();
   SPart part = sfirst_part(beg, end, g);
   if (tma && threadIdx.x < 3) prefetch_tensormap(a.tmap + threadIdx.x);
+  // the first preload's boxes into L2 while the previous kernel finishes
+  if (tma) prefetch_preload<HALO, 3>(a.tmap, part, g);
   grid_dependency_wait();
   grid_launch_dependents();
   auto stage_rows = [&](const SStage& st) {
