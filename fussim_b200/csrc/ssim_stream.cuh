@@ -304,17 +304,25 @@ __device__ __forceinline__ void finish_reduction(const FwdParams& a, bool failed
   const bool l1 = a.l1 != 0;
   __syncthreads();
   if (threadIdx.x == 0) {
-    if (failed) atomicOr(a.ticket + 1, 1u);  // the call's "failed" word
-    __threadfence();
-    const unsigned prev = atomicInc(a.ticket, gridDim.x - 1);
-    *s_last = (prev == gridDim.x - 1) ? 1u : 0u;
+    // One atomic per CTA on the ticket word: finished CTAs counted in its low 16 bits,
+    // CTAs that gave up in its high 16 bits (grids stay below 2^16 CTAs, checked on the
+    // host). Its release half orders this CTA's accumulator atomics before the count; its
+    // acquire half, in the last CTA, orders every counted CTA's before what follows. The
+    // last CTA leaves the word zero for the next call (the "failed" word after it is not
+    // used by these kernels and stays zero).
+    const unsigned add = failed ? 0x10001u : 1u;
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;\n"
+                 : "=r"(prev)
+                 : "l"(a.ticket), "r"(add)
+                 : "memory");
+    const bool last = (prev & 0xffffu) == gridDim.x - 1;
+    if (last) *a.ticket = 0u;
+    *s_last = !last ? 0u : ((prev >> 16) != 0u || failed) ? 2u : 1u;
   }
   __syncthreads();
   if (!*s_last) return;
   __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) *s_last = atomicExch(a.ticket + 1, 0u) != 0u ? 2u : 1u;
-  __syncthreads();
   const double poison = *s_last == 2u ? __longlong_as_double(0x7ff8000000000000ll) : 0.0;
   double local = 0.0, local_l1 = 0.0;
   for (int b = threadIdx.x; b < a.g.B; b += NT) {
