@@ -267,6 +267,7 @@ int launch_fwd(const fssim::FwdParams& p, cudaStream_t stream) {
   if (st) return st;
   const int grid = grid_size(p.g, occ, sms);
   if ((p.g.LT + grid - 1) / grid + 2 * p.g.H > INT_MAX) return fail(FSSIM_ERR_SHAPE, "batch too large");
+  if (grid >= 65536) return fail(FSSIM_ERR_CUDA, "grid too large for the reduction ticket");
   fssim::FwdParams q = p;
   q.wait_limit = g_wait_limit.load(std::memory_order_relaxed);
   const cudaError_t e = launch_pdl(k, grid, Cfg::kSmem, stream, q);

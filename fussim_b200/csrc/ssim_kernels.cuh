@@ -31,7 +31,8 @@
 // FP64 across the block), converts the run's sum to 2^-28 fixed point and adds it with
 // a 64-bit integer atomic into a per-image accumulator. Integer addition is associative,
 // so the result is bitwise deterministic in any CTA order. The last CTA to finish
-// (atomicInc ticket) turns the accumulators into the outputs and zeroes them again.
+// (the count on the ticket word reaches the grid size) turns the accumulators into the
+// outputs and zeroes them again.
 #pragma once
 
 #include <cuda.h>  // CUtensorMap (type only; the driver API is not linked)
@@ -1100,16 +1101,23 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   if (!a.reduce) return;
   __syncthreads();
   if (threadIdx.x == 0) {
-    if (failed) atomicOr(a.ticket + 1, 1u);  // the call's "failed" word
-    __threadfence();
-    const unsigned prev = atomicInc(a.ticket, gridDim.x - 1);
-    s_last = (prev == gridDim.x - 1) ? 1u : 0u;
+    // One atomic per CTA on the ticket word: finished CTAs in its low 16 bits, CTAs that
+    // gave up in its high 16 bits (grids stay below 2^16 CTAs, checked on the host). Its
+    // release half orders this CTA's accumulator atomics before the count, its acquire
+    // half (last CTA) every counted CTA's before what follows; the last CTA re-zeroes it.
+    const unsigned add = failed ? 0x10001u : 1u;
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;\n"
+                 : "=r"(prev)
+                 : "l"(a.ticket), "r"(add)
+                 : "memory");
+    const bool last = (prev & 0xffffu) == gridDim.x - 1;
+    if (last) *a.ticket = 0u;
+    s_last = !last ? 0u : ((prev >> 16) != 0u || failed) ? 2u : 1u;
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  if (threadIdx.x == 0) s_last = atomicExch(a.ticket + 1, 0u) != 0u ? 2u : 1u;
-  __syncthreads();
   // a CTA of this call gave up: every output of the call is NaN (the accumulators are
   // still zeroed for the next call)
   const double poison = s_last == 2u ? __longlong_as_double(0x7ff8000000000000ll) : 0.0;
