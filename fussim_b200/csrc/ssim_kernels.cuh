@@ -574,6 +574,22 @@ __device__ __forceinline__ void stage_tma_lanes(T* sm, const CUtensorMap* maps, 
   }
 }
 
+// L2 prefetch of the boxes stage_tma_lanes would copy for step s (thread l < NMAP * nbox
+// takes box l), issued before the wait for the previous kernel so the first staging hits
+// L2. A hint: coordinates are clamped to the image.
+template <typename StepT, int NMAP>
+__device__ __forceinline__ void prefetch_step_boxes(const CUtensorMap* maps, const StepT& s,
+                                                    int H) {
+  const int nbox = (s.nh() + kBoxRows - 1) / kBoxRows;
+  const int l = static_cast<int>(threadIdx.x);
+  if (l < NMAP * nbox) {
+    const int m = l / nbox;
+    const int b = l - m * nbox;
+    tma_prefetch_3d(maps + m, max(s.strip * kStrip - kLeft, 0),
+                    min(max(s.h0() + b * kBoxRows, 0), H - 1), s.plane);
+  }
+}
+
 // Copy ring rows [kRows, kRows + 2*HALO) to [0, 2*HALO): the vertical halo for the next
 // step. Only full steps carry, and 2*HALO <= kRows, so source and destination are disjoint
 // contiguous blocks.
@@ -888,6 +904,8 @@ __global__ void __launch_bounds__(kThreads, (FwdConfig<HALO, TIn, TP, TRAIN, MER
   __syncthreads();
   Step<HALO> cur = first_step<HALO>(beg, end, g);
   if (tma && threadIdx.x < 2) prefetch_tensormap(a.tmap + threadIdx.x);
+  // the first step's boxes into L2 while the previous kernel finishes
+  if (tma && cur.n) prefetch_step_boxes<Step<HALO>, 2>(a.tmap, cur, static_cast<int>(g.H));
   grid_dependency_wait();
   grid_launch_dependents();
   // TMA staging of a step by warp 0: lane 0 posts the byte count, the lanes issue the boxes
@@ -1277,6 +1295,8 @@ __global__ void __launch_bounds__(kThreads, (BwdConfig<HALO, TIn, TP, DLMAP>::kM
   __syncthreads();
   Step<HALO> cur = first_step<HALO>(beg, end, g);
   if (tma && threadIdx.x < (DLMAP ? 4 : 3)) prefetch_tensormap(a.tmap + threadIdx.x);
+  // the first step's partial boxes into L2 while the previous kernel finishes
+  if (tma && cur.n) prefetch_step_boxes<Step<HALO>, 3>(a.tmap, cur, static_cast<int>(g.H));
   grid_dependency_wait();
   grid_launch_dependents();
   // TMA staging of a step by warp 0: lane 0 posts the byte count, the lanes issue the boxes
